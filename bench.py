@@ -1,0 +1,435 @@
+"""MonarchAttention forward benchmark (B200).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME]
+                    [--impl ours|reference]
+
+One step = one MonarchAttention forward over the configuration's whole batch
+(default: the north-star config, E=4 H=16 N=16384 d=128 b=128 T=2 bf16).
+Under torchrun each rank runs its own full copy of the workload on its own GPU
+with its own seed (batch x heads sharded across GPUs, no collective on the
+data path): weak scaling, value = all ranks' tokens / max-over-ranks time.
+
+``--impl reference`` times the reference algorithm on the host CPU instead:
+the reference is Python (ma/ma_torch.py) and cannot be installed on the GPU
+box, so its CPU restatement in oracle/ma_oracle.py runs on all host cores
+(rank 0 only), on a bounded sample of heads per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MA fwd ms & tokens/s at N=16K d=128 H=16 bf16; % of HBM/tensor roofline"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default=None)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--kernel", default=None, help="force a kernel family: generic | tc")
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--verify", action="store_true",
+                    help="after timing, gather outputs to rank 0 (NCCL) and check heads")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU legs: the oracle port of ma/ma_torch.py on host cores
+# ---------------------------------------------------------------------------
+def cpu_sample(cfg, heads: int, threads: int, inputs=None):
+    """Run the oracle on `heads` (e, h) pairs of cfg in parallel; return seconds."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.ma_oracle import monarch_attention_oracle
+    try:
+        from threadpoolctl import threadpool_limits
+    except ImportError:  # pragma: no cover
+        threadpool_limits = None
+    if inputs is None:
+        inputs = cpu_inputs(cfg, heads)
+    q, k, v, mask, dt = inputs
+
+    def one(i):
+        e = i // cfg.H if mask is not None else 0
+        m = None if mask is None else mask[e:e + 1]
+        return monarch_attention_oracle(q[i:i + 1, None], k[i:i + 1, None], v[i:i + 1, None],
+                                        m, cfg.T, cfg.B, cfg.pre_pad, dt)
+
+    import contextlib
+    # one BLAS thread per worker: the parallelism is over heads
+    ctx = threadpool_limits(limits=1) if threadpool_limits else contextlib.nullcontext()
+    with ctx:
+        t0 = time.perf_counter()
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(one, range(heads)))
+        return time.perf_counter() - t0
+
+
+def cpu_inputs(cfg, heads):
+    """`heads` seeded (e, h) slices of cfg's inputs, as float32 numpy arrays
+    (16-bit / e4m3 values rounded exactly as the GPU sees them)."""
+    import numpy as np
+    import torch
+    from monarch_attention_b200.configs import dequantize_e4m3, make_inputs
+    small = cfg.with_(E=max(1, math.ceil(heads / cfg.H)), H=cfg.H)
+    q, k, v, mask, scales = make_inputs(small, device="cpu")
+    if scales is not None:
+        q, k, v = (dequantize_e4m3(t, s) for t, s in zip((q, k, v), scales))
+    flat = [t.float().reshape(-1, cfg.N, t.shape[-1])[:heads].numpy() for t in (q, k, v)]
+    dt = {"f32": "f32", "f16": "f16", "bf16": "bf16", "e4m3": "f32"}[cfg.dtype]
+    mk = None if mask is None else mask.numpy()
+    return flat[0], flat[1], flat[2], mk, dt
+
+
+def cpu_rate(cfg, threads, target_s, first_heads=None):
+    """Heads/s of the oracle on `threads` host threads, sampled for ~target_s."""
+    heads = first_heads or threads
+    inputs = cpu_inputs(cfg, heads)
+    t = cpu_sample(cfg, heads, threads, inputs)
+    reps = max(1, min(8, int(target_s / max(t, 1e-3))))
+    if reps > 1:
+        heads2 = min(heads * reps, cfg.E * cfg.H)
+        inputs = cpu_inputs(cfg, heads2)
+        t = cpu_sample(cfg, heads2, threads, inputs)
+        heads = heads2
+    return heads / t, heads, t
+
+
+def run_reference(args, cfg, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    heads = min(threads, cfg.E * cfg.H)
+    inputs = cpu_inputs(cfg, heads)
+    for _ in range(args.warmup):
+        cpu_sample(cfg, heads, threads, inputs)
+    times = []
+    for _ in range(args.steps):
+        times.append(cpu_sample(cfg, heads, threads, inputs))
+    per_step_sample = sum(times) / len(times)
+    full_step = per_step_sample * (cfg.E * cfg.H) / heads
+    tokens = cfg.E * cfg.N
+    value = tokens / full_step
+    sample = (f"{heads} of {cfg.E * cfg.H} (e,h) heads per step on {threads} host threads "
+              f"({cfg.dtype} emulated by the oracle port), scaled to the full batch")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": full_step * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
+        "config": config_dict(cfg),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+def config_dict(cfg, extra=None):
+    d = {"workload": cfg.name, "E": cfg.E, "H": cfg.H, "N": cfg.N, "D": cfg.D, "Dv": cfg.dv,
+         "block_size": cfg.B, "num_steps": cfg.T, "mask": cfg.mask_min_len is not None,
+         "pre_pad": cfg.pre_pad}
+    if extra:
+        d.update(extra)
+    return d
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"ma_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        sm = []
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+            except ValueError:
+                pass
+            for i, n in enumerate(names):
+                if r[5 + i].lower().startswith("active"):
+                    reasons.add(n)
+        sm.sort()
+        try:
+            smax = float(rows[-1][2])
+        except ValueError:
+            smax = None
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def flops_and_bytes(cfg):
+    """Algorithmic FLOPs and HBM bytes of one forward (padded length for FLOPs)."""
+    M = cfg.M
+    Np = M * cfg.B
+    D, Dv, B, T = cfg.D, cfg.dv, cfg.B, cfg.T
+    per_head = ((T - 1) * (4 * Np * B * D + 4 * Np * M * D) + 4 * Np * B * D
+                + 2 * Np * B * Dv + 2 * Np * M * D + 2 * Np * M * Dv)
+    heads = cfg.E * cfg.H
+    in_b = {"f32": 4, "f16": 2, "bf16": 2, "e4m3": 1}[cfg.dtype]
+    out_b = 4 if cfg.dtype == "f32" else 2
+    mask_b = cfg.E * cfg.N if cfg.mask_min_len is not None else 0
+    byts = heads * cfg.N * (2 * D + Dv) * in_b + heads * cfg.N * Dv * out_b + mask_b
+    return float(heads * per_head), float(byts)
+
+
+def run_gpu(args, cfg, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import monarch_attention_b200 as mab
+    from monarch_attention_b200 import _lib
+    from monarch_attention_b200.configs import make_inputs
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # every rank owns its own shard of batch x heads (its own seed)
+    q, k, v, mask, scales = make_inputs(cfg, device=dev, seed=cfg.seed + 7919 * rank)
+    impl = args.kernel
+    out = torch.empty((cfg.E, cfg.H, cfg.N, cfg.dv),
+                      dtype=torch.bfloat16 if cfg.dtype == "e4m3" else q.dtype, device=dev)
+    kernel_family = mab.selected_impl(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, impl=impl)
+
+    def fwd():
+        return mab.monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, impl=impl,
+                                     scales=scales, out=out)
+
+    in_bytes = sum(t.numel() * t.element_size() for t in (q, k, v))
+    flush = in_bytes < 2 * L2_BYTES
+    scrub = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
+
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        fwd()
+    launches_per_fwd = _lib.load().ma_last_launch_count()
+    barrier()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    time.sleep(0.15)
+    barrier()
+    if flush:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for i in range(args.steps):
+            scrub.fill_(float(i))
+            evs[i][0].record(stream)
+            fwd()
+            evs[i][1].record(stream)
+        barrier()
+        elapsed = sum(a.elapsed_time(b) for a, b in evs)
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fwd()
+        e1.record(stream)
+        barrier()
+        elapsed = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    status = mab.read_status(dev)
+    t = torch.tensor([elapsed], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    tokens_step = cfg.E * cfg.N * world
+    value = tokens_step / (ms_step / 1e3)
+
+    # ---- end to end through the public API: host (pinned) -> device -> host
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        hm = None if mask is None else mask.cpu().pin_memory()
+        hsc = None if scales is None else tuple(s.cpu() for s in scales)
+        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        n_e2e = args.e2e_steps or max(3, min(args.steps, 10))
+
+        def e2e_step():
+            dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+            dm = None if hm is None else hm.to(dev, non_blocking=True)
+            dsc = None if hsc is None else tuple(s.to(dev, non_blocking=True) for s in hsc)
+            o = mab.monarch_attention(dq, dk, dv, dm, cfg.T, cfg.B, cfg.pre_pad, impl=impl,
+                                      scales=dsc)
+            hout.copy_(o, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        b.record(stream)
+        barrier()
+        te = torch.tensor([a.elapsed_time(b)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_ms = float(te.item()) / n_e2e
+        h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
+        h2d += 0 if hm is None else hm.numel() * hm.element_size()
+        e2e = {"value": tokens_step / (e2e_ms / 1e3), "unit": "tokens/s",
+               "ms_per_step": e2e_ms, "steps": n_e2e,
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": hout.numel() * hout.element_size()}
+
+    if args.verify and world > 1:
+        gathered = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(gathered, out)
+        torch.cuda.synchronize()
+
+    # ---- roofline of the dominant kernel (one forward = one launch on tc)
+    peaks, peak_src = load_peaks()
+    flop, byts = flops_and_bytes(cfg)
+    t_s = ms_step / 1e3
+    if cfg.dtype == "f32":
+        peak_flops = 148 * 128 * 2 * 1.965e9
+        peak_note = "FFMA peak 148 SM x 128 lanes x 2 x 1.965 GHz (fp32 config)"
+    else:
+        peak_flops = peaks["bf16_tflops"] * 1e12 * (2 if cfg.dtype == "e4m3" else 1)
+        peak_note = f"bf16 dense burst, {peak_src}" + (" x2 (fp8 assumed)" if cfg.dtype == "e4m3" else "")
+    hbm = peaks["hbm_gbs"] * 1e9
+    t_flop, t_hbm = flop / peak_flops, byts / hbm
+    if t_flop >= t_hbm:
+        roof = {"bound": "tensor", "achieved": flop / t_s / 1e12, "peak": peak_flops / 1e12,
+                "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": byts / t_s / 1e9, "peak": hbm / 1e9, "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["peak_source"] = peak_note if roof["bound"] == "tensor" else f"hbm copy, {peak_src}"
+    roof["traffic"] = load_traffic(cfg.name, kernel_family)
+    roof["t_star_us"] = max(t_flop, t_hbm) * 1e6
+    roof["algorithmic_flop_per_launch"] = flop
+    roof["algorithmic_bytes_per_launch"] = byts
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, heads, secs = cpu_rate(cfg, threads, args.cpu_seconds)
+        full = (cfg.E * cfg.H) / rate
+        cpu = {"value": cfg.E * cfg.N / full, "unit": "tokens/s", "cores": threads,
+               "kind": "port",
+               "sample": f"{heads} (e,h) heads of {cfg.name} in {secs:.1f} s on {threads} "
+                         f"host threads (oracle port of ma/ma_torch.py), scaled to the batch"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": cfg.dtype, "data": "synthetic (seeded iid normal, per-rank seed)",
+            "config": config_dict(cfg, {
+                "kernel": kernel_family, "parallelism": f"batch x heads over {world} GPU(s)",
+                "l2": ("L2 flushed between timed steps (256 MB write, outside the events)"
+                       if flush else f"inputs larger than L2 ({in_bytes / 2**20:.0f} MiB)")}),
+            "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+            "gpu_launches": launches_per_fwd * args.steps, "clocks": clk,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def load_traffic(name, kernel):
+    """DRAM bytes per launch of the dominant kernel from a committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        d = json.load(f)
+    ent = d.get(f"{name}/{kernel}")
+    return None if ent is None else ent.get("dram_bytes_per_launch")
+
+
+def main():
+    args = parse()
+    from monarch_attention_b200.configs import CONFIGS, NORTH_STAR
+    cfg = CONFIGS[args.config or NORTH_STAR]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, cfg, rank, world)
+        return
+    run_gpu(args, cfg, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

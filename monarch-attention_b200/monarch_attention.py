@@ -1,0 +1,266 @@
+"""MonarchAttention operator surface backed by the sm_100a CUDA library.
+
+Drop-in for the reference module ``ma/monarch_attention.py`` of
+djmmoss/monarch-attention:
+
+  * ``PadType``                       <- ma/monarch_attention.py:12-14
+  * ``MonarchAttention(block_size, num_steps, pad_type, impl=None)``
+                                      <- ma/monarch_attention.py:17-37
+  * ``MonarchAttention.forward(query, key, value, attention_mask=None)``
+                                      <- ma/monarch_attention.py:39-58
+  * ``MonarchAttention.get_matrix(query, key, attention_mask=None)``
+                                      <- ma/monarch_attention.py:60-70
+  * ``monarch_attention(q, k, v, attn_mask, T, B, pre_pad)``
+                                      <- ma/ma_torch.py:65-73
+
+The ViT / RoBERTa / BART / DiT hooks call ``attn_module(q, k, v[, mask])`` with
+(E, H, N, D) views of arbitrary strides (vit/model.py:97,
+roberta/model.py:104-106, bart/model.py:150-152,
+dit/attention_processor.py:143); those calls work unchanged.  The work runs
+on the current CUDA stream through ``ma_fwd`` (include/ma_api.h).  Tensors on
+any other device raise: there is no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from enum import StrEnum
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+Tensor = torch.Tensor
+
+_TORCH_TO_MA = {
+    torch.float32: _lib.DTYPE_F32,
+    torch.float16: _lib.DTYPE_F16,
+    torch.bfloat16: _lib.DTYPE_BF16,
+    torch.float8_e4m3fn: _lib.DTYPE_E4M3,
+}
+_MASK_DTYPES = {
+    torch.bool: _lib.MASK_BOOL,
+    torch.uint8: _lib.MASK_BOOL,
+    torch.int8: _lib.MASK_BOOL,
+    torch.int32: _lib.MASK_I32,
+    torch.int64: _lib.MASK_I64,
+    torch.float32: _lib.MASK_F32,
+    torch.float16: _lib.MASK_F16,
+    torch.bfloat16: _lib.MASK_BF16,
+}
+_IMPL_ARG = {
+    None: _lib.IMPL_AUTO,
+    "auto": _lib.IMPL_AUTO,
+    # the reference's own names: both are replaced by the B200 kernels
+    "torch": _lib.IMPL_AUTO,
+    "triton": _lib.IMPL_AUTO,
+    "generic": _lib.IMPL_GENERIC,
+    "tc": _lib.IMPL_TC,
+}
+
+
+class PadType(StrEnum):
+    pre = "pre"
+    post = "post"
+
+
+_status_lock = threading.Lock()
+_status_words: dict[int, Tensor] = {}
+
+
+def status_word(device: torch.device) -> Tensor:
+    """Per-device int32 word into which kernels OR failure bits (MA_STATUS_*)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _status_lock:
+        w = _status_words.get(idx)
+        if w is None:
+            w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+            _status_words[idx] = w
+        return w
+
+
+def read_status(device: torch.device | None = None, reset: bool = True) -> int:
+    """Synchronously read (and by default clear) the device status word."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    w = status_word(device)
+    val = int(w.item())
+    if reset and val:
+        w.zero_()
+    return val
+
+
+def _impl_code(impl) -> int:
+    env = os.environ.get("MA_IMPL")
+    if env:
+        impl = env
+    if impl not in _IMPL_ARG:
+        raise ValueError(f"impl must be one of {sorted(k for k in _IMPL_ARG if k)}; got {impl!r}")
+    return _IMPL_ARG[impl]
+
+
+def _mask_arg(attn_mask: Tensor | None, E: int, N: int, device) -> tuple:
+    if attn_mask is None:
+        return None, (0, 0), _lib.MASK_NONE, None
+    if attn_mask.shape != (E, N):
+        raise ValueError(f"attention_mask must have shape (E, N) = {(E, N)}; "
+                         f"got {tuple(attn_mask.shape)}")
+    if attn_mask.device != device:
+        raise ValueError("attention_mask must be on the same device as the inputs")
+    keep = attn_mask
+    code = _MASK_DTYPES.get(attn_mask.dtype)
+    if code is None:  # any other dtype: nonzero = valid
+        keep = attn_mask != 0
+        code = _lib.MASK_BOOL
+    return keep.data_ptr(), tuple(keep.stride()), code, keep
+
+
+def build_params(q: Tensor, k: Tensor, v: Tensor, out: Tensor, attn_mask: Tensor | None,
+                 T: int, B: int, pre_pad: bool, impl: int = _lib.IMPL_AUTO,
+                 scales: tuple | None = None) -> tuple[_lib.MaFwdParams, list]:
+    """Fill an ``ma_fwd_params`` block; returns it and the tensors it points into."""
+    E, H, N, D = q.shape
+    Dv = v.shape[-1]
+    mptr, mstride, mcode, mkeep = _mask_arg(attn_mask, E, N, q.device)
+    p = _lib.MaFwdParams()
+    p.q, p.k, p.v, p.out = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    for name, t in (("q_stride", q), ("k_stride", k), ("v_stride", v), ("o_stride", out)):
+        arr = getattr(p, name)
+        for i, s in enumerate(t.stride()):
+            arr[i] = s
+    p.mask = mptr
+    p.mask_stride[0], p.mask_stride[1] = mstride
+    p.mask_dtype = mcode
+    p.E, p.H, p.N, p.D, p.Dv = E, H, N, D, Dv
+    p.block_size, p.num_steps, p.pre_pad = int(B), int(T), int(bool(pre_pad))
+    p.dtype = _TORCH_TO_MA[q.dtype]
+    p.out_dtype = _TORCH_TO_MA[out.dtype]
+    keep = [q, k, v, out, mkeep]
+    if scales is not None:
+        qs, ks, vs = (s.to(device=q.device, dtype=torch.float32).contiguous() for s in scales)
+        p.q_scale, p.k_scale, p.v_scale = qs.data_ptr(), ks.data_ptr(), vs.data_ptr()
+        keep += [qs, ks, vs]
+    p.impl = impl
+    return p, keep
+
+
+def _check_inputs(q: Tensor, k: Tensor, v: Tensor) -> None:
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("query, key and value must be 4-D (batch, heads, tokens, head_dim)")
+    if k.shape != q.shape:
+        raise ValueError(f"key shape {tuple(k.shape)} != query shape {tuple(q.shape)}")
+    if v.shape[:3] != q.shape[:3]:
+        raise ValueError(f"value shape {tuple(v.shape)} does not match query {tuple(q.shape)}")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise TypeError(f"query/key/value dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
+    if q.dtype not in _TORCH_TO_MA:
+        raise TypeError(f"unsupported dtype {q.dtype}")
+    for t in (q, k, v):
+        if t.device.type != "cuda":
+            raise RuntimeError("MonarchAttention (B200) runs on CUDA tensors only; "
+                               f"got a tensor on {t.device}")
+    if not (q.device == k.device == v.device):
+        raise ValueError("query/key/value are on different devices")
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        raise RuntimeError("MonarchAttention (B200) implements the forward pass only; "
+                           "call it under torch.no_grad() or torch.inference_mode()")
+
+
+def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int,
+                      B: int, pre_pad: bool, *, impl=None, scales: tuple | None = None,
+                      out: Tensor | None = None) -> Tensor:
+    """MonarchAttention forward on the current CUDA stream.
+
+    Same arguments and result as ``monarch_attention_torch``
+    (ma/ma_torch.py:65-108): q, k (E, H, N, D), v (E, H, N, Dv), optional
+    (E, N) mask (nonzero = valid), T alternating steps, block size B, and
+    pre_pad selecting front padding.  Returns a new contiguous (E, H, N, Dv)
+    tensor in v.dtype (bf16 for float8_e4m3fn inputs, which also need
+    ``scales=(q_scale, k_scale, v_scale)``, each (E, H) fp32).
+    """
+    _check_inputs(q, k, v)
+    E, H, N, _ = q.shape
+    Dv = v.shape[-1]
+    out_dtype = torch.bfloat16 if q.dtype == torch.float8_e4m3fn else v.dtype
+    if q.dtype == torch.float8_e4m3fn and scales is None:
+        raise ValueError("float8_e4m3fn inputs need scales=(q_scale, k_scale, v_scale)")
+    if out is None:
+        out = torch.empty((E, H, N, Dv), dtype=out_dtype, device=q.device)
+    lib = _lib.load()
+    p, keep = build_params(q, k, v, out, attn_mask, T, B, pre_pad, _impl_code(impl), scales)
+    nbytes = lib.ma_workspace_bytes(ctypes.byref(p))
+    if nbytes == 0:
+        _lib.check(lib.ma_fwd(ctypes.byref(p), None))  # raises with the reason
+    with torch.cuda.device(q.device):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
+        p.status = status_word(q.device).data_ptr()
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        nvtx = os.environ.get("MA_NVTX") == "1"
+        if nvtx:
+            torch.cuda.nvtx.range_push(f"monarch_attention E{E} H{H} N{N} B{B} T{T}")
+        rc = lib.ma_fwd(ctypes.byref(p), ctypes.c_void_p(stream))
+        if nvtx:
+            torch.cuda.nvtx.range_pop()
+    _lib.check(rc)
+    del keep
+    return out
+
+
+def selected_impl(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int, B: int,
+                  pre_pad: bool, impl=None) -> str:
+    """Name of the kernel family ``monarch_attention`` would run ("generic" / "tc")."""
+    lib = _lib.load()
+    out = torch.empty((1,), device=q.device)
+    p, _keep = build_params(q, k, v, out, attn_mask, T, B, pre_pad, _impl_code(impl))
+    p.out_dtype = p.dtype if p.dtype != _lib.DTYPE_E4M3 else _lib.DTYPE_BF16
+    for i, s in enumerate((q.shape[1] * q.shape[2] * v.shape[-1], q.shape[2] * v.shape[-1],
+                           v.shape[-1], 1)):
+        p.o_stride[i] = s
+    rc = lib.ma_select_impl(ctypes.byref(p))
+    if rc < 0:
+        _lib.check(-rc)
+    return _lib.IMPL_NAMES[rc]
+
+
+class MonarchAttention(nn.Module):
+    """MonarchAttention (ma/monarch_attention.py:17-70) on B200 CUDA kernels.
+
+    ``impl``: None / "auto" (default) picks the fastest kernel for the shape;
+    "generic" or "tc" force a kernel family; the reference's "torch" and
+    "triton" are accepted and mean "auto".  The MA_IMPL environment variable
+    overrides it (for tests).
+    """
+
+    def __init__(self, block_size: int, num_steps: int, pad_type: PadType,
+                 impl: str | None = None):
+        super().__init__()
+        self.block_size = block_size
+        self.num_steps = num_steps
+        self.pad_type = pad_type
+        _impl_code(impl)  # validate early
+        self.impl = impl
+
+    def forward(self, query: Tensor, key: Tensor, value: Tensor,
+                attention_mask: Tensor | None = None) -> Tensor:
+        return monarch_attention(query, key, value, attention_mask, self.num_steps,
+                                 self.block_size, self.pad_type == PadType.pre, impl=self.impl)
+
+    def get_matrix(self, query: Tensor, key: Tensor,
+                   attention_mask: Tensor | None = None) -> Tensor:
+        """Dense (E, H, N, N) attention matrix: the forward with V = I (fp32 result).
+
+        The reference passes a float32 identity whatever the query dtype
+        (ma/monarch_attention.py:67-69).  Here the identity is built in the
+        query dtype (0 and 1 are exact in every dtype), so the y / z products
+        are rounded to the query dtype, and the result is returned as fp32.
+        """
+        batch_size, num_heads, seq_len, _ = query.shape
+        value = torch.eye(seq_len, device=query.device, dtype=query.dtype).expand(
+            batch_size, num_heads, seq_len, seq_len)
+        return self.forward(query, key, value, attention_mask).float()
+
+    def extra_repr(self) -> str:
+        return (f"block_size={self.block_size}, num_steps={self.num_steps}, "
+                f"pad_type={self.pad_type}, impl={self.impl}")

@@ -1,0 +1,80 @@
+"""The CPU oracle against the reference's own outputs (golden fixtures made by
+tests/golden/gen_golden.py running ma/ma_torch.py), plus structural checks."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import golden_paths
+from gen_golden import load_case
+from oracle.ma_oracle import (flops, monarch_attention_oracle,
+                              monarch_attention_oracle_heads, round_to)
+
+
+@pytest.mark.parametrize("path", golden_paths(), ids=lambda p: os.path.basename(p)[:-4])
+def test_oracle_matches_reference(path):
+    c = load_case(path)
+    m = c["meta"]
+    args = (c["q"], c["k"], c["v"], c.get("mask"), m["T"], m["B"], m["pre_pad"])
+    out = monarch_attention_oracle(*args, dtype=m["dtype"])
+    out32 = monarch_attention_oracle(*args, dtype="f32")
+    scale = np.abs(c["out_ref_f32"]).max()
+    # fp32: same algorithm, same fp32 arithmetic -> agreement to rounding noise
+    assert np.abs(out32 - c["out_ref_f32"]).max() <= 1e-6 * max(scale, 1.0)
+    if m["dtype"] == "f32":
+        assert np.abs(out - c["out_ref"]).max() <= 1e-6 * max(scale, 1.0)
+    else:
+        # 16-bit emulation: identical rounding points; an fp32 summation-order
+        # difference may flip a rounding, so allow a few output ulps.
+        ulp = 2.0 ** -8 if m["dtype"] == "bf16" else 2.0 ** -11
+        assert np.abs(out - c["out_ref"]).max() <= 4 * ulp * scale
+    assert np.isfinite(out).all()
+
+
+def test_oracle_heads_loop_is_exact():
+    c = load_case(os.path.join(os.path.dirname(__file__), "golden", "roberta_mask_bf16.npz"))
+    m = c["meta"]
+    args = (c["q"], c["k"], c["v"], c.get("mask"), m["T"], m["B"], m["pre_pad"], "f32")
+    a = monarch_attention_oracle(*args)
+    b = monarch_attention_oracle_heads(*args)
+    assert np.abs(a - b).max() <= 1e-6
+
+
+def test_bf16_rounding_is_nearest_even():
+    x = np.array([1.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -2.5, np.inf, 1e-40], np.float32)
+    r = round_to(x, "bf16")
+    assert r[0] == 1.0 and r[1] == 1.0 and r[2] == 1.0 + 2 ** -6
+    assert r[3] == -2.5 and np.isinf(r[4])
+
+
+def test_matrix_rows_sum_to_one():
+    """With V = I the output is the Monarch matrix A; its rows sum to 1
+    (L is a softmax over k and each R block is row-stochastic)."""
+    rng = np.random.default_rng(0)
+    E, H, N, D, B = 1, 2, 64, 16, 8
+    q = rng.standard_normal((E, H, N, D)).astype(np.float32) / 4
+    k = rng.standard_normal((E, H, N, D)).astype(np.float32) / 4
+    eye = np.broadcast_to(np.eye(N, dtype=np.float32), (E, H, N, N))
+    A = monarch_attention_oracle(q, k, eye, None, 2, B, False)
+    assert np.abs(A.sum(-1) - 1.0).max() < 1e-5
+    assert (A >= 0).all()
+
+
+def test_fully_masked_sequence_has_no_nan():
+    rng = np.random.default_rng(1)
+    E, H, N, D, B = 2, 1, 40, 8, 8
+    q, k, v = (rng.standard_normal((E, H, N, D)).astype(np.float32) for _ in range(3))
+    mask = np.ones((E, N), bool)
+    mask[1] = False
+    out = monarch_attention_oracle(q, k, v, mask, 3, B, False)
+    assert np.isfinite(out).all()
+
+
+@pytest.mark.parametrize("N,B,T,ref", [(1024, 32, 3, 1.96e9), (2048, 32, 2, 3.93e9),
+                                       (4096, 64, 2, 10.9e9), (8192, 64, 2, 31.4e9)])
+def test_flop_count_matches_reference_figures(N, B, T, ref):
+    """figures/data.txt:3 lists MonarchAttention FLOPs of a BART-base encoder
+    layer (H=12, d=64) as counted by the reference's tooling; those values are
+    3x the algorithmic count."""
+    f = flops(1, 12, N, 64, 64, B, T) * 3
+    assert abs(f - ref) / ref < 0.01

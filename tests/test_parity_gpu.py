@@ -1,0 +1,206 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle and with the
+reference's own outputs (golden fixtures).
+
+Tolerances (from the task's north star): fp32 within 1e-4 max-abs of the
+fp32 reference; bf16 / fp16 within 2e-2 * max|ref| of the fp32 reference run
+on the same (rounded) inputs; e4m3 against the fp32 oracle on the
+dequantised inputs within E4M3_TOL * max|ref| (stated bound).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_paths
+from gen_golden import load_case
+import monarch_attention_b200 as mab
+from monarch_attention_b200 import MonarchAttention, PadType, monarch_attention
+from monarch_attention_b200.configs import CONFIGS, dequantize_e4m3, make_inputs
+from oracle.ma_oracle import monarch_attention_oracle, monarch_attention_oracle_heads
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-4
+LP_TOL = 2e-2
+E4M3_TOL = 6e-2
+TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+
+
+def tol_for(dtype, ref):
+    scale = float(np.abs(ref).max())
+    return F32_TOL if dtype == "f32" else LP_TOL * scale
+
+
+def to_dev(a, dtype, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev).to(TORCH_DT[dtype])
+
+
+def check_status(dev):
+    assert mab.read_status(dev) == 0
+
+
+# ---------------------------------------------------------------------------
+# golden fixtures (outputs of the reference itself)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("impl", ["auto", "generic"])
+@pytest.mark.parametrize("path", golden_paths(), ids=lambda p: os.path.basename(p)[:-4])
+def test_golden(path, impl, cuda_device):
+    c = load_case(path)
+    m = c["meta"]
+    dt = m["dtype"]
+    q, k, v = (to_dev(c[n], dt, cuda_device) for n in ("q", "k", "v"))
+    mask = None if "mask" not in c else torch.from_numpy(c["mask"]).to(cuda_device)
+    out = monarch_attention(q, k, v, mask, m["T"], m["B"], m["pre_pad"], impl=impl)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    got = out.float().cpu().numpy()
+    ref32 = c["out_ref_f32"]
+    assert out.dtype == q.dtype and out.shape == (m["E"], m["H"], m["N"], m["Dv"])
+    assert np.isfinite(got).all()
+    err = np.abs(got - ref32).max()
+    assert err <= tol_for(dt, ref32), f"max|err|={err:.3g}"
+
+
+# ---------------------------------------------------------------------------
+# the benchmark configs, reduced to a few heads (oracle in seconds)
+# ---------------------------------------------------------------------------
+SMALL = {
+    "cfg0_f32": dict(),
+    "vit_bf16": dict(E=2, H=2),
+    "roberta_bf16": dict(E=3, H=2),
+    "dit_bf16": dict(E=1, H=2),
+    "long4k_bf16": dict(E=1, H=2),
+    "long16k_bf16": dict(E=1, H=1),
+}
+
+
+def oracle_for(q, k, v, mask, cfg, dt):
+    qn, kn, vn = (t.float().cpu().numpy() for t in (q, k, v))
+    mn = None if mask is None else mask.cpu().numpy()
+    return monarch_attention_oracle_heads(qn, kn, vn, mn, cfg.T, cfg.B, cfg.pre_pad, dt)
+
+
+@pytest.mark.parametrize("impl", ["auto", "generic"])
+@pytest.mark.parametrize("name", list(SMALL))
+def test_config_small(name, impl, cuda_device):
+    cfg = CONFIGS[name].with_(**SMALL[name])
+    q, k, v, mask, _ = make_inputs(cfg, device="cpu")
+    out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                            None if mask is None else mask.to(cuda_device),
+                            cfg.T, cfg.B, cfg.pre_pad, impl=impl)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    ref = oracle_for(q, k, v, mask, cfg, "f32")
+    got = out.float().cpu().numpy()
+    err = np.abs(got - ref).max()
+    assert err <= tol_for(cfg.dtype, ref), f"{name}/{impl}: max|err|={err:.3g}"
+
+
+# ---------------------------------------------------------------------------
+# full-size configs: every head computed, a sample of heads checked exactly
+# ---------------------------------------------------------------------------
+FULL = ["cfg0_f32", "vit_bf16", "roberta_bf16", "dit_bf16", "long4k_bf16", "long16k_bf16"]
+
+
+@pytest.mark.parametrize("name", FULL)
+def test_config_full_size(name, cuda_device):
+    cfg = CONFIGS[name]
+    q, k, v, mask, _ = make_inputs(cfg, device=cuda_device)
+    out = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert torch.isfinite(out).all()
+    # heads are independent: check the first and the last (e, h) exactly
+    for e, h in ((0, 0), (cfg.E - 1, cfg.H - 1)):
+        sl = (slice(e, e + 1), slice(h, h + 1))
+        m = None if mask is None else mask[e:e + 1]
+        ref = oracle_for(q[sl], k[sl], v[sl], m, cfg, "f32")
+        got = out[sl].float().cpu().numpy()
+        err = np.abs(got - ref).max()
+        assert err <= tol_for(cfg.dtype, ref), f"{name} head ({e},{h}): max|err|={err:.3g}"
+
+
+# ---------------------------------------------------------------------------
+# interface behaviour
+# ---------------------------------------------------------------------------
+def test_permuted_views_match_contiguous(cuda_device):
+    """Hooks pass permute(0, 2, 1, 3) views of (E, N, H, D) projections."""
+    g = torch.Generator(device="cpu").manual_seed(7)
+    E, N, H, D = 2, 96, 3, 32
+    x = [torch.randn(E, N, H, D, generator=g).to(cuda_device, torch.bfloat16) for _ in range(3)]
+    views = [t.permute(0, 2, 1, 3) for t in x]
+    a = monarch_attention(*views, None, 2, 16, False)
+    b = monarch_attention(*[t.contiguous() for t in views], None, 2, 16, False)
+    assert torch.equal(a, b)
+    assert a.is_contiguous()
+
+
+def test_mask_dtypes_agree(cuda_device):
+    g = torch.Generator(device="cpu").manual_seed(8)
+    E, H, N, D = 2, 2, 80, 16
+    q, k, v = (torch.randn(E, H, N, D, generator=g).to(cuda_device) for _ in range(3))
+    mb = torch.ones(E, N, dtype=torch.bool)
+    mb[0, 50:] = False
+    mb[1, :7] = False
+    mb = mb.to(cuda_device)
+    outs = [monarch_attention(q, k, v, mb.to(dt), 2, 16, False)
+            for dt in (torch.bool, torch.int64, torch.int32, torch.float32, torch.float16,
+                       torch.bfloat16, torch.uint8)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    ref = monarch_attention_oracle(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(),
+                                   mb.cpu().numpy(), 2, 16, False)
+    assert np.abs(outs[0].cpu().numpy() - ref).max() <= F32_TOL
+
+
+def test_get_matrix_rows_sum_to_one(cuda_device):
+    g = torch.Generator(device="cpu").manual_seed(9)
+    E, H, N, D = 1, 2, 64, 32
+    q, k = (torch.randn(E, H, N, D, generator=g).to(cuda_device) / 4 for _ in range(2))
+    A = MonarchAttention(8, 2, PadType.post).get_matrix(q, k)
+    assert A.shape == (E, H, N, N) and A.dtype == torch.float32
+    assert (A.sum(-1) - 1).abs().max().item() < 1e-5
+    ref = monarch_attention_oracle(q.cpu().numpy(), k.cpu().numpy(),
+                                   np.broadcast_to(np.eye(N, dtype=np.float32), (E, H, N, N)),
+                                   None, 2, 8, False)
+    assert np.abs(A.cpu().numpy() - ref).max() <= F32_TOL
+
+
+def test_module_forward_matches_function(cuda_device):
+    cfg = CONFIGS["vit_bf16"].with_(E=1, H=2)
+    q, k, v, _, _ = make_inputs(cfg, device=cuda_device)
+    mod = MonarchAttention(cfg.B, cfg.T, PadType.post)
+    assert torch.equal(mod(q, k, v), monarch_attention(q, k, v, None, cfg.T, cfg.B, False))
+
+
+def test_deterministic(cuda_device):
+    cfg = CONFIGS["roberta_bf16"].with_(E=2, H=2)
+    q, k, v, mask, _ = make_inputs(cfg, device=cuda_device)
+    a = monarch_attention(q, k, v, mask, cfg.T, cfg.B, False)
+    b = monarch_attention(q, k, v, mask, cfg.T, cfg.B, False)
+    assert torch.equal(a, b)
+
+
+def test_fully_masked_rows_are_finite(cuda_device):
+    g = torch.Generator(device="cpu").manual_seed(10)
+    E, H, N, D = 2, 1, 64, 16
+    q, k, v = (torch.randn(E, H, N, D, generator=g) for _ in range(3))
+    mask = torch.ones(E, N, dtype=torch.bool)
+    mask[1] = False
+    mask[0, 16:32] = False
+    out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                            mask.to(cuda_device), 3, 16, False)
+    ref = monarch_attention_oracle(q.numpy(), k.numpy(), v.numpy(), mask.numpy(), 3, 16, False)
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert np.abs(got - ref).max() <= F32_TOL
+
+
+def test_missing_library_fails_loudly(monkeypatch, cuda_device):
+    from monarch_attention_b200 import _lib
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setattr(_lib, "LIB_PATH", "/nonexistent/libmonarch_attn.so")
+    q = torch.randn(1, 1, 16, 8, device=cuda_device)
+    with pytest.raises(RuntimeError, match="not built"):
+        monarch_attention(q, q, q, None, 2, 4, False)
