@@ -45,6 +45,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="target CPU time of the cpu_baseline sample")
+    ap.add_argument("--E", type=int, default=None, help="override the batch size (profiling)")
+    ap.add_argument("--H", type=int, default=None, help="override the head count (profiling)")
     ap.add_argument("--verify", action="store_true",
                     help="after timing, gather outputs to rank 0 (NCCL) and check heads")
     return ap.parse_args()
@@ -422,6 +424,8 @@ def main():
     args = parse()
     from monarch_attention_b200.configs import CONFIGS, NORTH_STAR
     cfg = CONFIGS[args.config or NORTH_STAR]
+    if args.E or args.H:
+        cfg = cfg.with_(E=args.E or cfg.E, H=args.H or cfg.H)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
