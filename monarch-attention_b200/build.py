@@ -44,12 +44,18 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(d) <= t for d in _deps())
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile every .cu under csrc/ into libmonarch_attn.so; returns its path."""
-    if not force and up_to_date():
-        return OUT
-    tmp = OUT + ".tmp"
-    cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-o", tmp, *sources()]
+def build(force: bool = False, verbose: bool = False, out: str = OUT,
+          defines: tuple = ()) -> str:
+    """Compile every .cu under csrc/ into libmonarch_attn.so; returns its path.
+
+    ``defines`` adds -D flags (e.g. ("MA_TC_TRACE",) for the per-item timeline
+    build, written to a separate ``out`` path).
+    """
+    if not force and out == OUT and up_to_date():
+        return out
+    tmp = out + ".tmp"
+    cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *[f"-D{d}" for d in defines], "-I", INCLUDE,
+           "-o", tmp, *sources()]
     res = subprocess.run(cmd, capture_output=True, text=True)
     log = os.path.join(HERE, "build.log")
     with open(log, "w") as f:
@@ -58,8 +64,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
         raise RuntimeError(f"nvcc failed (see {log}):\n{res.stderr[-4000:]}")
     if verbose:
         print(res.stderr)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":

@@ -8,7 +8,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/ma_api.h"
+#include "ma_api.h"
 
 namespace ma {
 

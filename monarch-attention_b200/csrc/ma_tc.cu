@@ -20,18 +20,23 @@
 // the output phase of the head that used it before), so the live set stays
 // L2-resident.
 //
-// CTA roles (192 threads, one CTA per SM):
-//   warps 0-3  softmax + epilogue; thread i owns row i = TMEM lane i
-//   warp 4     scheduler + TMA producer (2-stage SMEM ring)
-//   warp 5     TMEM allocator + tcgen05.mma issuer
-// Per item:
-//   GEMM1  S = A * B^T            (both K-major, SW128 SMEM tiles) -> TMEM
-//   softmax over the row (fp32, exp2), P -> TMEM as bf16 (R / out items) or
-//          -> SMEM in the MN-major SW128 layout (L items, whose second GEMM
-//          contracts over rows)
-//   GEMM2  O = P * X  (A from TMEM)   or   O = P^T * Q_j (A MN-major SMEM)
-//          plus cr = P^T * 1 on L items (N = 16 GEMM against a ones tile)
-//   epilogue: TMEM -> registers -> scale -> bf16 -> global
+// CTA roles (384 threads = 3 warpgroups, one CTA per SM):
+//   warpgroups 0, 1  softmax + epilogue; group g takes the items n with
+//                    n % 2 == g (ping-pong), thread i owns row i = TMEM lane i
+//   warp 8           scheduler + TMA producer (3-entry ring, 2 tiles each)
+//   warp 9           TMEM allocator + tcgen05.mma issuer
+// The softmax streams each row out of TMEM in 64-column halves, so every
+// thread fits in the 168 registers a 384-thread CTA gets.
+// Per item n (group g = n % 2, ring entry e = n % 3):
+//   GEMM1  S[g] = A * B^T        (A, B: K-major SW128 tiles of entry e)
+//   softmax over the row (fp32, exp2); P -> TMEM S[g] as 16-bit (R / out
+//          items) or -> the B tile of entry e (free after GEMM1) in the
+//          MN-major SW128 layout (L items, whose GEMM2 contracts over rows)
+//   GEMM2  O[g] = P * X           (A from TMEM; X = K[m] or y_j)
+//          O[g] = P^T * Q_j       (L items; and cr = P^T * 1 into S[g])
+//   R-final items run a second part O[g] = P * V[m]; V and y_j are loaded
+//   into the A tile of the entry once GEMM1 has consumed it.
+//   epilogue: TMEM -> registers -> scale -> 16-bit -> global
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <stdlib.h>
@@ -42,31 +47,45 @@
 namespace ma {
 namespace tc {
 
-constexpr int kThreads = 192;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kThreads = 480;
+constexpr int kEpiWarp0 = 8;       // warps 8-11: epilogue warpgroup
+constexpr int kProducerWarp = 12;
+constexpr int kMmaWarp = 13;
+constexpr int kStoreWarp = 14;     // TMA stores + publication
 constexpr int kT = 128;                  // tile edge: b = M = D = 128
 constexpr int kHalf = 16384;             // one 64-column half of a tile (128 rows x 128 B)
 constexpr int kTileBytes = 2 * kHalf;    // 32 KB
-constexpr int kStageBytes = 3 * kTileBytes;
+constexpr int kEntries = 3;              // ring entries (items in flight)
+constexpr int kEntryBytes = 2 * kTileBytes;  // tiles A and B
+constexpr int kItemRing = 8;             // item descriptors for the epilogue
+constexpr int kScaleRing = 4;            // per-row output scales, softmax -> epilogue
 // small objects at the start of dynamic shared memory
-constexpr int kOffBar = 0;        // mbarriers (16 x 8 B)
-constexpr int kOffDesc = 128;     // item descriptors (2 x int4)
-constexpr int kOffTmem = 160;     // TMEM base address
-constexpr int kOffVec = 256;      // per stage: cr[m][:] or cl[j][:] of the item (2 x 512 B)
-constexpr int kOffOnes = 1280;    // ones operand of the cr GEMM (512 B)
-constexpr int kSmallBytes = 1792;
-// 1024-aligned tile region (SW128 atoms): 2 stages x {A, B, X}, then P^T
-constexpr int kTileOffP = 2 * kStageBytes;
-constexpr int kTileRegion = kTileOffP + kTileBytes;
+constexpr int kOffBar = 0;        // mbarriers
+constexpr int kOffDesc = 256;     // item descriptors of the ring entries (kEntries x int4)
+constexpr int kOffEnd = 320;      // number of items this CTA was given (set at the end)
+constexpr int kOffTmem = 324;     // TMEM base address
+constexpr int kOffItems = 384;    // item descriptors by item index (kItemRing x int4)
+constexpr int kOffVec = 512;      // per entry: cr[m][:] or cl[j][:] (kEntries x 512 B)
+constexpr int kOffOnes = 2048;    // ones operand of the cr GEMM (512 B)
+constexpr int kOffScale = 2560;   // output scale per row (kScaleRing x 128 fp32)
+constexpr int kSmallBytes = kOffScale + kScaleRing * 512;
+constexpr int kTileRegion = kEntries * kEntryBytes;
 constexpr int kSmemBytes = kSmallBytes + 1024 + kTileRegion;  // + worst-case alignment pad
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-// TMEM columns (fp32 accumulators, 128 lanes)
-constexpr uint32_t kColS = 0;     // S, then P (bf16 pairs) in its first 64 columns
-constexpr uint32_t kColO1 = 128;  // al / ar / z accumulator
-constexpr uint32_t kColO2 = 256;  // y accumulator (final R-step)
-constexpr uint32_t kColCr = 384;  // cr accumulator (L-step), 16 columns
+// barrier offsets (8 B each)
+constexpr int kBarFull = 0;      // [kEntries] A/B tiles (+ vector) of the entry landed
+constexpr int kBarEmpty = 24;    // [kEntries] the entry's last GEMM finished
+constexpr int kBarX = 48;        // [kEntries] late X tile (V or y) landed
+constexpr int kBarSFull = 72;    // [2] S of the group written (GEMM1 done)
+constexpr int kBarPReady = 88;   // [2] P of the group written (128 arrivals)
+constexpr int kBarOFull = 104;   // [2] O of the group written (one per GEMM2 part)
+constexpr int kBarOFree = 120;   // [2] O of the group read (128 arrivals per part)
+constexpr int kBarCrTaken = 136; // [2] cr read out of S (L items, 128 arrivals)
+constexpr int kBarDrain = 160;   // MMA drain before the end
+constexpr int kBarStaged = 168;  // [kEntries] output tile(s) of the entry's item staged (128)
+
+// TMEM columns (fp32, 128 lanes): per group g, S/P at 256 g and O at 256 g + 128
 constexpr uint32_t kTmemCols = 512;
 
 // control block (uint32 words in the workspace)
@@ -85,6 +104,10 @@ struct TcParams {
   CUtensorMap tm_al;    // al rows [slot][j][m]
   CUtensorMap tm_ar;    // ar rows [slot][m][j]
   CUtensorMap tm_y;     // y rows  [slot][j][m]
+  CUtensorMap tm_al_st; // al as (D, M, slots*b): 64 x 1 x 128 boxes = rows j of block m
+  CUtensorMap tm_y_st;  // y, same view
+  CUtensorMap tm_ar_st; // ar as (D, b, slots*M): rows k of index j
+  CUtensorMap tm_out_st;// out as (Dv, b, M, H, E): tokens l*b + j of index j
   void* out;
   int64_t os[4];
   char* al;
@@ -97,6 +120,7 @@ struct TcParams {
   int H, nheads, T, P, slots;
   float sm_scale;
   unsigned long long timeout_ns;
+  unsigned long long* trace;  // MA_TC_TRACE builds: per-CTA item timestamps, else null
 };
 
 enum Kind : int { KIND_R = 0, KIND_L = 1, KIND_O = 2 };
@@ -130,6 +154,16 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -171,6 +205,33 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* tm,
       "[%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap* tm, uint32_t src, int c0, int c1,
+                                             int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
                                             int c2, int c3, int c4, uint32_t bar) {
@@ -335,6 +396,25 @@ __device__ __noinline__ bool wait_counter(const uint32_t* ctr, uint32_t target, 
   }
 }
 
+// Optional per-item timeline (compiled in with -DMA_TC_TRACE): for the first
+// kTraceItems items of each CTA, slot 0 holds (head, phase, item) and slots
+// 1..7 globaltimer stamps: 1 claim, 2 dependency met, 3 GEMM1 issued,
+// 4 softmax start, 5 P ready, 6 epilogue start, 7 published; 8.. softmax
+// internals (row 0): 8 late-X issued, 9 pass-1 first TMEM wait, 10 pass 1
+// done, 11 pass-2 first TMEM wait, 12 pass 2 done, 13 pass 3 done,
+// 14 first epilogue TMEM wait, 15 epilogue stores done.
+constexpr int kTraceItems = 256;
+constexpr int kTraceSlots = 16;
+__device__ __forceinline__ void trace_stamp(const TcParams& p, uint32_t n, int slot,
+                                            unsigned long long v) {
+#ifdef MA_TC_TRACE
+  if (p.trace != nullptr && n < (uint32_t)kTraceItems)
+    p.trace[((size_t)blockIdx.x * kTraceItems + n) * kTraceSlots + slot] = v;
+#else
+  (void)p; (void)n; (void)slot; (void)v;
+#endif
+}
+
 // warp-uniform bounded wait: every lane waits, and the warp goes on only if
 // all lanes saw the phase complete (so .sync.aligned tcgen05 ops that follow
 // are executed by the whole warp or by none of it)
@@ -367,20 +447,91 @@ __device__ __forceinline__ void store_row32(char* dst, const uint32_t (&o)[32], 
 }
 
 // 128 TMEM accumulator columns of this lane -> scaled 16-bit row of 256 B
+// (64 columns per TMEM round trip)
 template <bool BF16>
 __device__ __forceinline__ void store_row128(char* dst, uint32_t taddr, float scale) {
 #pragma unroll
-  for (int q4 = 0; q4 < 4; ++q4) {
-    uint32_t o[32];
-    tmem_ld32(taddr + q4 * 32, o);
+  for (int h2 = 0; h2 < 2; ++h2) {
+    uint32_t o[2][32];
+    tmem_ld32(taddr + h2 * 64, o[0]);
+    tmem_ld32(taddr + h2 * 64 + 32, o[1]);
     tmem_wait_ld();
-    store_row32<BF16>(dst + q4 * 64, o, scale);
+    store_row32<BF16>(dst + h2 * 128, o[0], scale);
+    store_row32<BF16>(dst + h2 * 128 + 64, o[1], scale);
+  }
+}
+
+// 128 TMEM accumulator columns of this lane -> scaled 16-bit row of an output
+// tile staged in SMEM in the SW128 layout the TMA store expects: row r of
+// half h at h*16K + r*128, 16-byte chunk c at position c ^ (r & 7)
+template <bool BF16>
+__device__ __forceinline__ void stage_row128(uint32_t tile, int row, uint32_t taddr, float scale) {
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    uint32_t o[2][32];
+    tmem_ld32(taddr + h2 * 64, o[0]);
+    tmem_ld32(taddr + h2 * 64 + 32, o[1]);
+    tmem_wait_ld();
+    const uint32_t rbase = tile + h2 * kHalf + row * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        w[t] = pack2<BF16>(__uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t]) * scale,
+                           __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t + 1]) * scale);
+      st_shared_v4(rbase + ((c ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
+// packed fp32 pairs (sm_100 f32x2 pipe ops)
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+template <bool BF16>
+__device__ __forceinline__ void gemm1(uint32_t tS, uint32_t A, uint32_t B) {
+  constexpr uint32_t id_ss = idesc_f16(BF16, false, false, 128, 128);  // S = A B^T
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;  // K step of 16 inside SW128 rows
+    mma_ss(tS, smem_desc(A + off, 16, 1024, kSwz128), smem_desc(B + off, 16, 1024, kSwz128),
+           id_ss, kk > 0);
+  }
+}
+// O = P (TMEM, 128 x 128 16-bit) * X (SMEM, MN-major SW128 128 x 128)
+template <bool BF16>
+__device__ __forceinline__ void gemm2_ts(uint32_t tO, uint32_t tP, uint32_t X) {
+  constexpr uint32_t id_ts = idesc_f16(BF16, false, true, 128, 128);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    mma_ts(tO, tP + kk * 8, smem_desc(X + kk * 2048, kHalf, 1024, kSwz128), id_ts, kk > 0);
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constant__ TcParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -393,29 +544,30 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
   const int P = p.P;
   const uint32_t total = (uint32_t)p.nheads * P * kT;
 
-  const uint32_t bar_full0 = sbase + kOffBar + 0;    // +8 * stage
-  const uint32_t bar_empty0 = sbase + kOffBar + 16;  // +8 * stage
-  const uint32_t bar_sfull = sbase + kOffBar + 32;
-  const uint32_t bar_pready = sbase + kOffBar + 40;
-  const uint32_t bar_ofull = sbase + kOffBar + 48;
-  const uint32_t bar_ofree = sbase + kOffBar + 56;
-  const uint32_t bar_drain = sbase + kOffBar + 64;
-  const uint32_t bar_epi = sbase + kOffBar + 72;
   int4* desc_slot = reinterpret_cast<int4*>(smem_raw + kOffDesc);
+  int4* item_ring = reinterpret_cast<int4*>(smem_raw + kOffItems);
+  volatile uint32_t* n_end_s = reinterpret_cast<volatile uint32_t*>(smem_raw + kOffEnd);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem_raw + kOffTmem);
   const float* vec0 = reinterpret_cast<const float*>(smem_raw + kOffVec);
+  float* scale_ring = reinterpret_cast<float*>(smem_raw + kOffScale);
+  auto bar = [&](int off, int i) { return sbase + kOffBar + off + 8 * i; };
 
   if (tid == 0) {
-    mbar_init(bar_full0, 1);
-    mbar_init(bar_full0 + 8, 1);
-    mbar_init(bar_empty0, 1);
-    mbar_init(bar_empty0 + 8, 1);
-    mbar_init(bar_sfull, 1);
-    mbar_init(bar_pready, 128);
-    mbar_init(bar_ofull, 1);
-    mbar_init(bar_ofree, 128);
-    mbar_init(bar_drain, 1);
-    mbar_init(bar_epi, 128);
+    for (int i = 0; i < kEntries; ++i) {
+      mbar_init(bar(kBarFull, i), 1);
+      mbar_init(bar(kBarEmpty, i), 1);
+      mbar_init(bar(kBarX, i), 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(kBarSFull, g), 1);
+      mbar_init(bar(kBarPReady, g), 128);
+      mbar_init(bar(kBarOFull, g), 1);
+      mbar_init(bar(kBarOFree, g), 128);
+      mbar_init(bar(kBarCrTaken, g), 128);
+    }
+    for (int i = 0; i < kEntries; ++i) mbar_init(bar(kBarStaged, i), 128);
+    mbar_init(bar(kBarDrain, 0), 1);
+    *n_end_s = 0xFFFFFFFFu;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kMmaWarp) {
@@ -438,16 +590,17 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
   if (warp == kProducerWarp) {
     // ===================== scheduler + TMA producer =====================
     if (lane == 0) {
-      // wavefront cursor over valid (round r, phase ph) blocks; blk = index
-      int r = 0, ph = 0;
+      int r = 0, ph = 0;  // wavefront cursor: round, phase; blk = its block index
       uint32_t blk = 0;
-      bool issued[2] = {false, false};  // a load was issued on the stage
-      uint32_t last_on[2] = {0, 0};     // item counter of the last load on it
+      uint32_t issued = 0;  // bit e: a load was issued on entry e
+      uint32_t last_on[kEntries] = {0, 0, 0};
       uint32_t n = 0;
       for (;; ++n) {
-        const int s = n & 1;
-        const uint32_t fb = bar_full0 + 8 * s;
-        if (n >= 2 && !wait_bar(bar_empty0 + 8 * s, ((n >> 1) - 1) & 1, guard)) break;
+        const int e = n % kEntries;
+        const uint32_t use = n / kEntries;
+        const uint32_t fb = bar(kBarFull, e);
+        if (n >= kEntries && !wait_bar(bar(kBarEmpty, e), (use - 1) & 1, guard)) break;
+        trace_stamp(p, n, 1, globaltimer());
         const uint32_t w = atomicAdd(ctrl + kCtrlNext, 1u);
         bool ok = w < total && !ld_relaxed(guard.abort);
         int head = -1, item = 0, kind = 0;
@@ -479,279 +632,441 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
                               guard);
         }
         if (!ok) {
-          desc_slot[s] = make_int4(-1, 0, 0, 0);  // end marker
+          *n_end_s = n;  // items n, n+1, ... do not exist
           mbar_arrive(fb);
           break;
         }
-        desc_slot[s] = make_int4(head, ph, item, kind);
+        desc_slot[e] = make_int4(head, ph, item, kind);
+        item_ring[n % kItemRing] = make_int4(head, ph, item, kind);
+        trace_stamp(p, n, 0, ((unsigned long long)head << 32) | ((unsigned)ph << 16) | item);
+        trace_stamp(p, n, 2, globaltimer());
         fence_proxy_async_global();
         const int slot = head % p.slots;
-        const int e = head / p.H, hh = head - e * p.H;
-        const uint32_t A = tbase + s * kStageBytes, B = A + kTileBytes, X = B + kTileBytes;
-        const uint32_t vdst = sbase + kOffVec + s * 512;
+        const int eb = head / p.H, hh = head - eb * p.H;
+        const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
+        const uint32_t vdst = sbase + kOffVec + e * 512;
         const size_t vrow = ((size_t)slot * kT + item) * kT;  // cr[slot][m][:] / cl[slot][j][:]
         if (kind == KIND_R) {
-          const bool first = ph == 0, final_ = ph == P - 2;
-          mbar_expect_tx(fb, (final_ ? 3 : 2) * kTileBytes + (first ? 0 : 512));
+          const bool first = ph == 0;
+          mbar_expect_tx(fb, 2 * kTileBytes + (first ? 0 : 512));
           if (!first) bulk_load(vdst, p.cr + vrow, 512, fb);
+#pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             if (first)
-              tma_load_4d(A + h2 * kHalf, &p.tm_qblk, h2 * 64, item * kT, hh, e, fb);
+              tma_load_4d(A + h2 * kHalf, &p.tm_qblk, h2 * 64, item * kT, hh, eb, fb);
             else
               tma_load_2d(A + h2 * kHalf, &p.tm_ar, h2 * 64, (slot * kT + item) * kT, fb);
-            tma_load_4d(B + h2 * kHalf, &p.tm_kblk, h2 * 64, item * kT, hh, e, fb);
-            if (final_) tma_load_4d(X + h2 * kHalf, &p.tm_vblk, h2 * 64, item * kT, hh, e, fb);
+            tma_load_4d(B + h2 * kHalf, &p.tm_kblk, h2 * 64, item * kT, hh, eb, fb);
           }
         } else {
-          const bool out = kind == KIND_O;
-          mbar_expect_tx(fb, (out ? 3 : 2) * kTileBytes + 512);
+          mbar_expect_tx(fb, 2 * kTileBytes + 512);
           bulk_load(vdst, p.cl + vrow, 512, fb);
+#pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
-            tma_load_5d(A + h2 * kHalf, &p.tm_qstr, h2 * 64, item, 0, hh, e, fb);
+            tma_load_5d(A + h2 * kHalf, &p.tm_qstr, h2 * 64, item, 0, hh, eb, fb);
             tma_load_2d(B + h2 * kHalf, &p.tm_al, h2 * 64, (slot * kT + item) * kT, fb);
-            if (out) tma_load_2d(X + h2 * kHalf, &p.tm_y, h2 * 64, (slot * kT + item) * kT, fb);
           }
         }
-        issued[s] = true;
-        last_on[s] = n;
+        issued |= 1u << e;
+        last_on[e] = use;
       }
       // never leave with copies in flight: after an abort, wait (bounded,
-      // ignoring the abort flag) until the last load of each stage landed
+      // ignoring the abort flag) until the last load of each entry landed
       if (ld_relaxed(guard.abort)) {
-        for (int s = 0; s < 2; ++s) {
-          if (!issued[s]) continue;
-          const uint32_t par = (last_on[s] >> 1) & 1;
+        for (int e = 0; e < kEntries; ++e) {
+          if (!(issued >> e & 1)) continue;
           const uint64_t t0 = globaltimer();
-          while (!mbar_try(bar_full0 + 8 * s, par) && globaltimer() - t0 < guard.limit) {
+          while (!mbar_try(bar(kBarFull, e), last_on[e] & 1) && globaltimer() - t0 < guard.limit) {
           }
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ===================== tcgen05.mma issuer =====================
+    // Non-blocking event loop: any item's loads may wait on earlier items of
+    // this CTA (dependencies are per phase), so the issuer never blocks on
+    // one condition while other issuable work exists.  GEMM1 of item m runs
+    // ahead (m <= n + 1: S of the group is free once GEMM2 of item m-2 was
+    // issued -- the tensor pipe executes MMAs in issue order).
     if (lane == 0) {
-      constexpr uint32_t id_ss = idesc_f16(BF16, false, false, 128, 128);  // S = A B^T
-      constexpr uint32_t id_ts = idesc_f16(BF16, false, true, 128, 128);   // O = P X
-      constexpr uint32_t id_mm = idesc_f16(BF16, true, true, 128, 128);    // ar = P^T Q_j
-      constexpr uint32_t id_cr = idesc_f16(BF16, true, false, 128, 16);    // cr = P^T 1
-      const uint32_t tS = tmem + kColS, tO1 = tmem + kColO1, tO2 = tmem + kColO2,
-                     tCr = tmem + kColCr;
-      const uint32_t Pt = tbase + kTileOffP;
+      constexpr uint32_t id_mm = idesc_f16(BF16, true, true, 128, 128);  // ar = P^T Q_j
+      constexpr uint32_t id_cr = idesc_f16(BF16, true, false, 128, 16);  // cr = P^T 1
       const uint32_t ones = sbase + kOffOnes;
-      int4 d = make_int4(-1, 0, 0, 0);
-      if (wait_bar(bar_full0, 0, guard)) d = desc_slot[0];
-      if (d.x >= 0) {
-        tc_fence_after();
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-          mma_ss(tS, smem_desc(tbase + off, 16, 1024, kSwz128),
-                 smem_desc(tbase + kTileBytes + off, 16, 1024, kSwz128), id_ss, kk > 0);
-        }
-        mma_commit(bar_sfull);
-        for (uint32_t n = 0;; ++n) {
-          const int s = n & 1;
-          const uint32_t A = tbase + s * kStageBytes, B = A + kTileBytes, X = B + kTileBytes;
-          if (!wait_bar(bar_pready, n & 1, guard)) break;
-          if (n > 0 && !wait_bar(bar_ofree, (n - 1) & 1, guard)) break;
-          tc_fence_after();
-          if (d.w == KIND_L) {
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint32_t off = kk * 2048;  // 16 rows l = two 8-row SW128 atoms
-              const uint64_t pd = smem_desc(Pt + off, kHalf, 1024, kSwz128);
-              mma_ss(tO1, pd, smem_desc(A + off, kHalf, 1024, kSwz128), id_mm, kk > 0);
-              mma_ss(tCr, pd, smem_desc(ones, 128, 256, kSwzNone), id_cr, kk > 0);
-            }
-          } else {
-            const bool final_ = d.w == KIND_R && d.y == P - 2;
-            const uint32_t Xo = d.w == KIND_O ? X : B;  // R: O1 = P K[m]; out: O1 = P y_j
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint32_t off = kk * 2048;
-              mma_ts(tO1, tS + kk * 8, smem_desc(Xo + off, kHalf, 1024, kSwz128), id_ts, kk > 0);
-              if (final_)
-                mma_ts(tO2, tS + kk * 8, smem_desc(X + off, kHalf, 1024, kSwz128), id_ts, kk > 0);
+      uint32_t m = 0;                     // next item for GEMM1
+      uint32_t n = 0;                     // next item for GEMM2
+      int part = 0;                       // GEMM2 parts of item n already issued
+      bool x_ok = false;                  // late X tile of item n observed
+      uint32_t n_end = 0xFFFFFFFFu;       // known once the end marker is seen
+      uint32_t parts[2] = {0, 0};         // O parts committed per group
+      uint32_t cr_waits[2] = {0, 0};      // cr_taken phases consumed per group
+      int prev_kind[2] = {-1, -1};        // kind of the group's previous item
+      uint32_t xcnt[kEntries] = {0, 0, 0};  // late-X phases consumed per entry
+      uint64_t t_last = globaltimer();
+      for (uint32_t spin = 0;; ++spin) {
+        bool progressed = false;
+        // ---- GEMM2 (one part) of item n ----
+        if (n < m) {
+          const int e = n % kEntries, g = n & 1;
+          const int4 d = desc_slot[e];
+          const bool two = d.w == KIND_R && d.y == P - 2;  // R-final: al part, then y part
+          const bool needx = d.w == KIND_O || (two && part == 1);
+          bool ready = part > 0 || mbar_test(bar(kBarPReady, g), (n >> 1) & 1);
+          if (ready && needx && !x_ok) {
+            ready = mbar_test(bar(kBarX, e), xcnt[e] & 1);
+            if (ready) {
+              x_ok = true;
+              ++xcnt[e];
             }
           }
-          mma_commit(bar_ofull);
-          mma_commit(bar_empty0 + 8 * s);
-          // next item's GEMM1 into S: the tensor pipe runs MMAs in issue
-          // order, so it starts after this item's GEMM2 has read P
-          const int s1 = (n + 1) & 1;
-          if (!wait_bar(bar_full0 + 8 * s1, ((n + 1) >> 1) & 1, guard)) break;
-          d = desc_slot[s1];
-          if (d.x < 0) {
-            mbar_arrive(bar_sfull);  // pass the end marker to the softmax warps
+          if (ready && parts[g] > 0) ready = mbar_test(bar(kBarOFree, g), (parts[g] - 1) & 1);
+          if (ready) {
+            tc_fence_after();
+            const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
+            const uint32_t tS = tmem + 256 * g, tO = tS + 128;
+            if (d.w == KIND_L) {
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint64_t pd = smem_desc(B + kk * 2048, kHalf, 1024, kSwz128);  // P^T
+                mma_ss(tO, pd, smem_desc(A + kk * 2048, kHalf, 1024, kSwz128), id_mm, kk > 0);
+                mma_ss(tS, pd, smem_desc(ones, 128, 256, kSwzNone), id_cr, kk > 0);
+              }
+            } else if (d.w == KIND_O || part == 1) {
+              gemm2_ts<BF16>(tO, tS, A);  // out: P y_j; R-final part 2: P V[m] (tile A)
+            } else {
+              gemm2_ts<BF16>(tO, tS, B);  // R: P K[m]
+            }
+            mma_commit(bar(kBarOFull, g));
+            ++parts[g];
+            if (++part == (two ? 2 : 1)) {
+              ++n;  // the epilogue releases the entry once its stores read the tiles
+              part = 0;
+              x_ok = false;
+            }
+            progressed = true;
+          }
+        }
+        // ---- GEMM1 of item m ----
+        if (m < n_end && m <= n + 1) {
+          const int e = m % kEntries, gm = m & 1;
+          if (mbar_test(bar(kBarFull, e), (m / kEntries) & 1)) {
+            if (m >= *n_end_s) {
+              n_end = m;
+            } else {
+              bool ok = true;
+              if (prev_kind[gm] == KIND_L) {  // its cr lives in S[gm]: wait until read
+                ok = mbar_test(bar(kBarCrTaken, gm), cr_waits[gm] & 1);
+                if (ok) {
+                  ++cr_waits[gm];
+                  prev_kind[gm] = -1;
+                }
+              }
+              if (ok) {
+                prev_kind[gm] = desc_slot[e].w;
+                tc_fence_after();
+                const uint32_t A = tbase + e * kEntryBytes;
+                gemm1<BF16>(tmem + 256 * gm, A, A + kTileBytes);
+                mma_commit(bar(kBarSFull, gm));
+                trace_stamp(p, m, 3, globaltimer());
+                ++m;
+                progressed = true;
+              }
+            }
+          }
+        }
+        if (n >= n_end) break;
+        if (progressed) {
+          t_last = globaltimer();
+        } else if ((spin & 255u) == 0) {
+          if (ld_relaxed(guard.abort)) break;
+          if (globaltimer() - t_last > guard.limit) {
+            guard.raise(MA_STATUS_WAIT_TIMEOUT);
             break;
           }
-          tc_fence_after();
-          const uint32_t A1 = tbase + s1 * kStageBytes, B1 = A1 + kTileBytes;
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-            mma_ss(tS, smem_desc(A1 + off, 16, 1024, kSwz128),
-                   smem_desc(B1 + off, 16, 1024, kSwz128), id_ss, kk > 0);
-          }
-          mma_commit(bar_sfull);
         }
-      } else {
-        mbar_arrive(bar_sfull);  // nothing to do (or gave up): pass the end marker on
       }
-      // let every issued MMA complete before TMEM is released
-      mma_commit(bar_drain);
+      // let every issued MMA complete, then pass the end marker on: one
+      // extra phase of S-full (softmax groups) and O-full (epilogue) each
+      mma_commit(bar(kBarDrain, 0));
       const uint64_t t0 = globaltimer();
-      while (!mbar_try(bar_drain, 0) && globaltimer() - t0 < guard.limit) {
+      while (!mbar_try(bar(kBarDrain, 0), 0) && globaltimer() - t0 < guard.limit) {
+      }
+      if (*n_end_s == 0xFFFFFFFFu) *n_end_s = n;  // gave up: stop everyone
+      // The softmax groups have observed every S-full phase (each item's
+      // P-ready was seen before its GEMM2), so one extra phase cannot alias.
+      mbar_arrive(bar(kBarSFull, 0));
+      mbar_arrive(bar(kBarSFull, 1));
+      // The epilogue may still be draining earlier items: an extra O-full
+      // phase landing before it observed the group's last real one would
+      // advance the barrier two phases and the parity wait would miss it.
+      // Wait (bounded) until the group's last O part was released first.
+      for (int g = 0; g < 2; ++g) {
+        if (parts[g] > 0) {
+          const uint64_t t1 = globaltimer();
+          while (!mbar_try(bar(kBarOFree, g), (parts[g] - 1) & 1) &&
+                 globaltimer() - t1 < guard.limit) {
+          }
+        }
+        mbar_arrive(bar(kBarOFull, g));
       }
     }
-  } else {
-    // ===================== softmax + epilogue (warps 0-3) =====================
-    const int row = tid;  // = TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const uint32_t tS = tmem + lane_off + kColS;
-    const uint32_t tO1 = tmem + lane_off + kColO1;
-    const uint32_t tO2 = tmem + lane_off + kColO2;
-    const uint32_t tCr = tmem + lane_off + kColCr;
-    for (uint32_t n = 0;; ++n) {
-      if (!wait_bar_warp(bar_sfull, n & 1, guard)) break;
-      const int4 d = desc_slot[n & 1];
-      if (d.x < 0) break;
-      // the stage's vector was written by the async proxy: observe its barrier
-      // (already complete -- the MMA warp waited on it before GEMM1)
-      if (!wait_bar_warp(bar_full0 + 8 * (n & 1), (n >> 1) & 1, guard)) break;
+  } else if (warp < 8) {
+    // ===================== softmax (warpgroups 0, 1) =====================
+    const int g = warp >> 2;
+    const int row = tid & 127;  // = TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + 256 * g + lane_off;
+    for (uint32_t k = 0;; ++k) {
+      const uint32_t n = 2 * k + g;
+      const int e = n % kEntries;
+      if (!wait_bar_warp(bar(kBarSFull, g), k & 1, guard)) break;
+      if (n >= *n_end_s) break;
+      // the entry's vector was written by the async proxy: observe its
+      // barrier (already complete -- GEMM1 consumed the entry)
+      if (!wait_bar_warp(bar(kBarFull, e), (n / kEntries) & 1, guard)) break;
       tc_fence_after();
+      if (row == 0) trace_stamp(p, n, 4, globaltimer());
+      const int4 d = desc_slot[e];
       const int head = d.x, ph = d.y, item = d.z, kind = d.w;
       const int slot = head % p.slots;
       const bool final_ = kind == KIND_R && ph == P - 2;
-      const float* vec = vec0 + (n & 1) * 128;  // cr[m][:] (R) or cl[j][:] (L / out)
+      const int eb = head / p.H, hh = head - eb * p.H;
+      const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
+      const float* vec = vec0 + e * 128;  // cr[m][:] (R) or cl[j][:] (L / out)
 
-      uint32_t sv[128];
-      tmem_ld32(tS + 0, *reinterpret_cast<uint32_t(*)[32]>(sv + 0));
-      tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-      tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(sv + 64));
-      tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(sv + 96));
-      tmem_wait_ld();
-
-      float sum = 0.0f, scale_out = 1.0f, cl_row = 0.0f;
-      if (kind == KIND_R) {
-        // t_i = sm_scale * S_i / (cr_j + eps); mx = max(max_i t_i, eps)
-        // (ma_torch.py:11-16), carried in log2 units: u_i = (t_i - mx) log2(e)
-        const float crj = ph > 0 ? vec[row] : 1.0f;
-        const float c = p.sm_scale / (crj + kEps);
-        float smax = -INFINITY;
+      // late X tile (V[m] for R-final, y_j for out) into tile A, free after GEMM1
+      if ((final_ || kind == KIND_O) && row == 0) {
+        fence_proxy_async_global();
+        const uint32_t xb = bar(kBarX, e);
+        mbar_expect_tx(xb, kTileBytes);
 #pragma unroll
-        for (int i = 0; i < 128; ++i) smax = fmaxf(smax, __uint_as_float(sv[i]));
-        const float mx = fmaxf(c * smax, kEps);
-        const float c2 = c * kLog2e, m2 = mx * kLog2e;
-        float wsum = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const float u = fmaf(__uint_as_float(sv[i]), c2, -m2);
-          const float e = ex2(u);
-          sum += e;
-          wsum = fmaf(e, u, wsum);
-          sv[i] = __float_as_uint(e);
+        for (int h2 = 0; h2 < 2; ++h2) {
+          if (final_)
+            tma_load_4d(A + h2 * kHalf, &p.tm_vblk, h2 * 64, item * kT, hh, eb, xb);
+          else
+            tma_load_2d(A + h2 * kHalf, &p.tm_y, h2 * 64, (slot * kT + item) * kT, xb);
         }
+      }
+
+      // The row of S (128 fp32) is streamed out of TMEM in 64-column halves:
+      // pass 1 takes the row maximum, pass 2 exponentiates and sums (P goes
+      // back to TMEM; for L items e goes back in place), pass 3 (L only)
+      // normalises and writes P^T to shared memory.
+      const bool rk = kind == KIND_R;
+      float c = 1.0f;  // R: sm_scale / (cr_j + eps)
+      if (rk) c = p.sm_scale / ((ph > 0 ? vec[row] : 1.0f) + kEps);
+      float mx;
+      {
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t sv[64];
+          tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
+          tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+          tmem_wait_ld();
+          if (rk) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[i]));
+          } else {
+            const float* cv = vec + 64 * h2;
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[i]) - cv[i]);
+          }
+        }
+        mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      }
+      // exponent arguments in log2 units: u = u_a * x + u_b
+      float u_a, u_b;
+      if (rk) {
+        // t_i = sm_scale * S_i / (cr_j + eps); mx = max(max_i t_i, eps) (ma_torch.py:11-16)
+        const float mxt = fmaxf(c * mx, kEps);
+        u_a = c * kLog2e;
+        u_b = -mxt * kLog2e;
+      } else {
+        u_a = kLog2e;  // x = S - cl[k]
+        u_b = -mx * kLog2e;
+      }
+      float s4[4] = {0.f, 0.f, 0.f, 0.f}, w4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t sv[64];
+        tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float x = __uint_as_float(sv[i]);
+          if (!rk) x -= vec[64 * h2 + i];
+          const float u = fmaf(x, u_a, u_b);
+          const float ev = ex2(u);
+          s4[i & 3] += ev;
+          if (rk) w4[i & 3] = fmaf(ev, u, w4[i & 3]);
+          sv[i] = __float_as_uint(ev);
+        }
+        if (kind == KIND_L) {  // e back in place (fp32), normalised in pass 3
+          tmem_st32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
+          tmem_st32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        } else {
+          // P (unnormalised) as packed 16-bit pairs into TMEM columns
+          // 32*h2 .. 32*h2+31: those S columns were already read
+          uint32_t pk[32];
+#pragma unroll
+          for (int c2 = 0; c2 < 32; ++c2)
+            pk[c2] = pack2<BF16>(__uint_as_float(sv[2 * c2]), __uint_as_float(sv[2 * c2 + 1]));
+          tmem_st32(tS + 32 * h2, pk);
+        }
+      }
+      tmem_wait_st();
+      const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      float scale_out;
+      if (rk) {
+        const float wsum = (w4[0] + w4[1]) + (w4[2] + w4[3]);
         const float den = sum + kEps;  // r = e / (sum + eps), :17
         const float inv = 1.0f / den;
         // cl = sum_i r_i log r_i, log r_i = (t_i - mx) - log(den)  (:20)
-        cl_row = kLn2 * inv * wsum - __logf(den) * sum * inv;
+        p.cl[((size_t)slot * kT + row) * kT + item] = kLn2 * inv * wsum - __logf(den) * sum * inv;
         scale_out = inv;
       } else {
-        // logits S'[l][k] - cl[j][k], softmax over k (ma_torch.py:27-29, 56-58)
-        float mx = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < 128; i += 4) {
-          const float4 c4 = *reinterpret_cast<const float4*>(vec + i);
-          const float u0 = __uint_as_float(sv[i + 0]) - c4.x;
-          const float u1 = __uint_as_float(sv[i + 1]) - c4.y;
-          const float u2 = __uint_as_float(sv[i + 2]) - c4.z;
-          const float u3 = __uint_as_float(sv[i + 3]) - c4.w;
-          sv[i + 0] = __float_as_uint(u0);
-          sv[i + 1] = __float_as_uint(u1);
-          sv[i + 2] = __float_as_uint(u2);
-          sv[i + 3] = __float_as_uint(u3);
-          mx = fmaxf(mx, fmaxf(fmaxf(u0, u1), fmaxf(u2, u3)));
-        }
-        const float m2 = mx * kLog2e;
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          const float e = ex2(fmaf(__uint_as_float(sv[i]), kLog2e, -m2));
-          sum += e;
-          sv[i] = __float_as_uint(e);
-        }
         scale_out = 1.0f / sum;
       }
+      scale_ring[(n % kScaleRing) * 128 + row] = scale_out;
 
       if (kind == KIND_L) {
-        // P[l][k] (normalised; every query row valid here) -> SMEM in the
-        // MN-major SW128 layout: row l of half h at h*16K + l*128, 16-byte
-        // chunk c at position c ^ (l & 7)
-        const uint32_t prow = tbase + kTileOffP + row * 128;
-#pragma unroll
+        // P[l][k] = e / sum (every query row valid here) -> tile B (al_j is
+        // consumed) in the MN-major SW128 layout: row l of half h at
+        // h*16K + l*128, 16-byte chunk c at position c ^ (l & 7)
+        const uint32_t prow = B + row * 128;
+#pragma unroll 1
         for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t sv[64];
+          tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
+          tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+          tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int k0 = h2 * 64 + c * 8;
+          for (int cc = 0; cc < 8; ++cc) {
             uint32_t a[4];
 #pragma unroll
             for (int t = 0; t < 4; ++t)
-              a[t] = pack2<BF16>(__uint_as_float(sv[k0 + 2 * t]) * scale_out,
-                                 __uint_as_float(sv[k0 + 2 * t + 1]) * scale_out);
-            st_shared_v4(prow + h2 * kHalf + ((c ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+              a[t] = pack2<BF16>(__uint_as_float(sv[cc * 8 + 2 * t]) * scale_out,
+                                 __uint_as_float(sv[cc * 8 + 2 * t + 1]) * scale_out);
+            st_shared_v4(prow + h2 * kHalf + ((cc ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
           }
         }
         fence_proxy_async_smem();
-      } else {
-        // P (unnormalised) -> TMEM columns 0..63 as packed 16-bit pairs
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          pk[c] = pack2<BF16>(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
-        tmem_st32(tS + 0, pk);
-#pragma unroll
-        for (int c = 0; c < 32; ++c)
-          pk[c] = pack2<BF16>(__uint_as_float(sv[64 + 2 * c]), __uint_as_float(sv[65 + 2 * c]));
-        tmem_st32(tS + 32, pk);
-        tmem_wait_st();
       }
       tc_fence_before();
-      mbar_arrive(bar_pready);
-
-      // ---------------- epilogue ----------------
-      if (!wait_bar_warp(bar_ofull, n & 1, guard)) break;
+      mbar_arrive(bar(kBarPReady, g));
+      if (row == 0) trace_stamp(p, n, 5, globaltimer());
+    }
+  } else if (warp < kEpiWarp0 + 4) {
+    // ===================== epilogue (warpgroup 2) =====================
+    // Drains O of both groups in item order: TMEM -> registers -> scale ->
+    // 16-bit -> SMEM staging in the item's own ring tiles (free once its
+    // GEMM2 ran); the store warp takes it from there.
+    const int row = tid & 127;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    uint32_t eparts[2] = {0, 0};  // O parts consumed per group
+    for (uint32_t n = 0;; ++n) {
+      const int g = n & 1, e = n % kEntries;
+      const uint32_t tS = tmem + 256 * g + lane_off, tO = tS + 128;
+      if (!wait_bar_warp(bar(kBarOFull, g), eparts[g] & 1, guard)) break;
+      if (n >= *n_end_s) break;
       tc_fence_after();
+      ++eparts[g];
+      if (row == 0) trace_stamp(p, n, 6, globaltimer());
+      const int4 d = item_ring[n % kItemRing];
+      const int head = d.x, ph = d.y, item = d.z, kind = d.w;
+      const int slot = head % p.slots;
+      const float scale_out = scale_ring[(n % kScaleRing) * 128 + row];
+      const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
+      const bool final_ = kind == KIND_R && ph == P - 2;
       if (kind == KIND_R) {
-        // al[j][m] = sm_scale * r K[m] (ma_torch.py:21); y[j][m] = r V[m] (:51)
-        const size_t orow = (((size_t)slot * kT + row) * kT + item) * kT * 2;
-        store_row128<BF16>(p.al + orow, tO1, p.sm_scale * scale_out);
-        if (final_) store_row128<BF16>(p.y + orow, tO2, scale_out);
-        p.cl[((size_t)slot * kT + row) * kT + item] = cl_row;  // cl[j][m]
+        // al[j][m] = sm_scale * r K[m] (ma_torch.py:21); R-final stages it in
+        // tile B (K is consumed) while its second GEMM2 part reads V in tile A
+        stage_row128<BF16>(final_ ? B : A, row, tO, p.sm_scale * scale_out);
+        if (final_) {
+          // y[j][m] = r V[m] (:51), second pass through O
+          tc_fence_before();
+          mbar_arrive(bar(kBarOFree, g));
+          if (!wait_bar_warp(bar(kBarOFull, g), eparts[g] & 1, guard)) break;
+          tc_fence_after();
+          ++eparts[g];
+          stage_row128<BF16>(A, row, tO, scale_out);
+        }
       } else if (kind == KIND_L) {
-        // ar[k][j] = sum_l P[l][k] q[l*b+j]; cr[k][j] = sum_l P[l][k] (:32-34)
-        const size_t orow = (((size_t)slot * kT + row) * kT + item) * kT * 2;
-        store_row128<BF16>(p.ar + orow, tO1, 1.0f);
+        // cr[k][j] = sum_l P[l][k] (the N = 16 GEMM into S[g]; read it first,
+        // then let the next GEMM1 of this group overwrite S[g]) (:32)
         uint32_t o[32];
-        tmem_ld32(tCr, o);  // the N = 16 accumulator; every column holds the sum
+        tmem_ld32(tS, o);
         tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(bar(kBarCrTaken, g));
         p.cr[((size_t)slot * kT + row) * kT + item] = __uint_as_float(o[0]);
+        // ar[k][j] = sum_l P[l][k] q[l*b+j] (:34)
+        stage_row128<BF16>(A, row, tO, 1.0f);
       } else {
         // z[l*b + j] = (P y_j) / sum (ma_torch.py:60-62)
-        const int e = head / p.H, hh = head - e * p.H;
-        char* dst = reinterpret_cast<char*>(p.out) +
-                    2 * ((int64_t)e * p.os[0] + (int64_t)hh * p.os[1] +
-                         (int64_t)(row * kT + item) * p.os[2]);
-        store_row128<BF16>(dst, tO1, scale_out);
+        stage_row128<BF16>(A, row, tO, scale_out);
       }
+      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(bar_ofree);
-      // publish the item once all 128 rows are stored
-      __threadfence();
-      mbar_arrive(bar_epi);
-      if (warp == 0) {  // lane 0 waits; the decision stays warp-uniform
-        bool ok = true;
-        if (lane == 0) {
-          ok = wait_bar(bar_epi, n & 1, guard);
-          if (ok) red_release_add(ctrl + kCtrlDone + head * P + ph, 1u);
+      mbar_arrive(bar(kBarOFree, g));
+      mbar_arrive(bar(kBarStaged, e));
+      if (row == 0) trace_stamp(p, n, 15, globaltimer());
+    }
+  } else if (warp == kStoreWarp) {
+    // ===================== TMA stores + publication =====================
+    // Per item: wait until its tiles are staged, store them, release the
+    // ring entry once the stores have read SMEM, and publish the item once
+    // its writes are complete.
+    if (lane == 0) {
+      // Publication is immediate: later phases of the head wait for the last
+      // item of this one, so any delay here lengthens the phase boundary.
+      for (uint32_t n = 0;; ++n) {
+        const int e = n % kEntries;
+        bool ready = false;
+        const uint64_t t0 = globaltimer();
+        for (uint32_t spin = 0;; ++spin) {
+          if (mbar_test(bar(kBarStaged, e), (n / kEntries) & 1)) {
+            ready = true;
+            break;
+          }
+          if (n >= *n_end_s) break;  // no such item
+          if ((spin & 63u) == 0) {
+            if (ld_relaxed(guard.abort)) break;
+            if (globaltimer() - t0 > guard.limit) {
+              guard.raise(MA_STATUS_WAIT_TIMEOUT);
+              break;
+            }
+          }
         }
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+        if (!ready) break;
+        const int4 d = item_ring[n % kItemRing];
+        const int head = d.x, ph = d.y, item = d.z, kind = d.w;
+        const int slot = head % p.slots;
+        const bool final_ = kind == KIND_R && ph == P - 2;
+        const int eb = head / p.H, hh = head - eb * p.H;
+        const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          if (kind == KIND_R) {
+            tma_store_3d(&p.tm_al_st, (final_ ? B : A) + h2 * kHalf, h2 * 64, item, slot * kT);
+            if (final_) tma_store_3d(&p.tm_y_st, A + h2 * kHalf, h2 * 64, item, slot * kT);
+          } else if (kind == KIND_L) {
+            tma_store_3d(&p.tm_ar_st, A + h2 * kHalf, h2 * 64, item, slot * kT);
+          } else {
+            tma_store_5d(&p.tm_out_st, A + h2 * kHalf, h2 * 64, item, 0, hh, eb);
+          }
+        }
+        bulk_commit();
+        bulk_wait_read<0>();  // staging read: the ring entry can be refilled
+        mbar_arrive(bar(kBarEmpty, e));
+        bulk_wait<0>();       // writes complete
+        fence_proxy_async_global();
+        red_release_add(ctrl + kCtrlDone + head * P + ph, 1u);
+        trace_stamp(p, n, 7, globaltimer());
       }
+      bulk_wait<0>();  // never leave with stores in flight
     }
   }
 
@@ -866,6 +1181,26 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
     const uint64_t stry[1] = {(uint64_t)s.Dv * 2};
     ok = ok && encode(&tp.tm_y, dt, 2, w + ws.y, dimy, stry, box_ws);
   }
+  {
+    // store views: 64 x 1 x 128 boxes of strided rows
+    const uint32_t box3[3] = {64, 1, kT};
+    const uint64_t dal[3] = {(uint64_t)s.D, (uint64_t)s.M, (uint64_t)slots * s.b};
+    const uint64_t sal[2] = {(uint64_t)s.D * 2, (uint64_t)s.M * s.D * 2};
+    ok = ok && encode(&tp.tm_al_st, dt, 3, w + ws.al, dal, sal, box3);
+    const uint64_t dy[3] = {(uint64_t)s.Dv, (uint64_t)s.M, (uint64_t)slots * s.b};
+    const uint64_t sy[2] = {(uint64_t)s.Dv * 2, (uint64_t)s.M * s.Dv * 2};
+    ok = ok && encode(&tp.tm_y_st, dt, 3, w + ws.y, dy, sy, box3);
+    const uint64_t dar[3] = {(uint64_t)s.D, (uint64_t)s.b, (uint64_t)slots * s.M};
+    const uint64_t sar[2] = {(uint64_t)s.D * 2, (uint64_t)s.b * s.D * 2};
+    ok = ok && encode(&tp.tm_ar_st, dt, 3, w + ws.ar, dar, sar, box3);
+    const int64_t* os = p->o_stride;
+    const uint64_t dout[5] = {(uint64_t)s.Dv, (uint64_t)s.b, (uint64_t)s.M, (uint64_t)s.H,
+                              (uint64_t)s.E};
+    const uint64_t sout[4] = {(uint64_t)os[2] * 2, (uint64_t)os[2] * 2 * s.b,
+                              (uint64_t)os[1] * 2, (uint64_t)os[0] * 2};
+    const uint32_t box5[5] = {64, 1, kT, 1, 1};
+    ok = ok && encode(&tp.tm_out_st, dt, 5, p->out, dout, sout, box5);
+  }
   if (!ok) return cudaErrorInvalidValue;
   tp.out = p->out;
   for (int i = 0; i < 4; ++i) tp.os[i] = p->o_stride[i];
@@ -885,6 +1220,10 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   tp.timeout_ns = 2000000000ull;  // 2 s per bounded wait
   const char* tmo = getenv("MA_WAIT_TIMEOUT_NS");
   if (tmo) tp.timeout_ns = strtoull(tmo, nullptr, 10);
+#ifdef MA_TC_TRACE
+  const char* trc = getenv("MA_TC_TRACE_PTR");  // device buffer of grid x 256 x 8 u64
+  if (trc) tp.trace = reinterpret_cast<unsigned long long*>(strtoull(trc, nullptr, 0));
+#endif
 
   int dev = 0, sms = 0;
   cudaError_t err = cudaGetDevice(&dev);
