@@ -128,6 +128,24 @@ size_t ma_workspace_bytes(const ma_fwd_params* p);
  * (replaces monarch_attention_torch, ma/ma_torch.py:65-108). */
 int ma_fwd(const ma_fwd_params* p, void* stream);
 
+/* Same forward as ma_fwd(), for callers that cannot allocate device memory
+ * (e.g. inside a stream capture that must not allocate, or a runtime whose
+ * memory pool forbids foreign allocations): the scratch comes from a 64 MiB
+ * array compiled into the library instead of p->workspace, which is ignored.
+ * No counterpart in the reference (its PyTorch implementation allocates its
+ * intermediates per call, ma/ma_torch.py:89).
+ *   - Runs the tcgen05 kernel only: block size = number of blocks = head dim
+ *     = 128, bf16 / fp16, no mask; other shapes, and shapes whose scratch
+ *     exceeds 64 MiB, return MA_ERR_UNSUPPORTED before anything runs.
+ *   - Every GPU that loads the library keeps the 64 MiB until process exit.
+ *   - All calls on a device share the array: calls that overlap on the GPU
+ *     race.  The array keeps the previous call's contents; each call clears
+ *     the part that must start at zero.
+ *   - The first call on a device performs a one-time set-up
+ *     (cudaGetSymbolAddress); make it before any stream capture.
+ *   - p->status may be NULL (device-side failures are then not reported). */
+int ma_fwd_noalloc(const ma_fwd_params* p, void* stream);
+
 /* Which implementation ma_fwd() would run for these params
  * (MA_IMPL_GENERIC or MA_IMPL_TC), or a negative error code. */
 int ma_select_impl(const ma_fwd_params* p);

@@ -134,6 +134,12 @@ int select_impl(const ma_fwd_params* p, const Shape& s, int* impl) {
 
 }  // namespace
 
+namespace ma {
+// Lets the allocation-free entry point (ma_noalloc.cu) report through
+// ma_last_error_detail().
+void set_error_detail(const std::string& detail) { g_detail = detail; }
+}  // namespace ma
+
 extern "C" {
 
 size_t ma_workspace_bytes(const ma_fwd_params* p) {

@@ -103,3 +103,17 @@ def test_impl_selection_is_host_only():
     assert lib.ma_select_impl(ctypes.byref(p)) == _lib.IMPL_GENERIC
     p.impl = _lib.IMPL_GENERIC
     assert lib.ma_select_impl(ctypes.byref(p)) == _lib.IMPL_GENERIC
+
+
+def test_noalloc_entry_rejects_on_the_host():
+    """ma_fwd_noalloc refuses shapes outside the tcgen05 kernel before any
+    CUDA call (no GPU needed)."""
+    lib = mab.load_library()
+    fn = lib.ma_fwd_noalloc
+    fn.argtypes = [ctypes.POINTER(_lib.MaFwdParams), ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    p = good_params()  # block size 16: generic shapes only
+    assert fn(ctypes.byref(p), None) == 7
+    assert b"tcgen05" in lib.ma_last_error_detail()
+    p = good_params(E=0)
+    assert fn(ctypes.byref(p), None) == 2
