@@ -47,11 +47,12 @@
 namespace ma {
 namespace tc {
 
-constexpr int kThreads = 480;
+constexpr int kThreads = 512;
 constexpr int kEpiWarp0 = 8;       // warps 8-11: epilogue warpgroup
 constexpr int kProducerWarp = 12;
 constexpr int kMmaWarp = 13;
-constexpr int kStoreWarp = 14;     // TMA stores + publication
+constexpr int kStoreWarp = 14;     // warps 14, 15: TMA stores + publication (alternate items)
+constexpr int kStoreWarps = 2;
 constexpr int kT = 128;                  // tile edge: b = M = D = 128
 constexpr int kHalf = 16384;             // one 64-column half of a tile (128 rows x 128 B)
 constexpr int kTileBytes = 2 * kHalf;    // 32 KB
@@ -118,6 +119,8 @@ struct TcParams {
   uint32_t* ctrl;
   uint32_t* status;
   int H, nheads, T, P, slots;
+  int hgroup;  // heads per wavefront phase slot (round r runs phase p of heads hgroup*(r-p) + i)
+  int early;   // 1: claim the next item (and await its dependency) before its ring entry frees
   float sm_scale;
   unsigned long long timeout_ns;
   unsigned long long* trace;  // MA_TC_TRACE builds: per-CTA item timestamps, else null
@@ -590,7 +593,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
   if (warp == kProducerWarp) {
     // ===================== scheduler + TMA producer =====================
     if (lane == 0) {
-      int r = 0, ph = 0;  // wavefront cursor: round, phase; blk = its block index
+      // wavefront cursor over valid (round r, phase ph, head sub) blocks of
+      // 128 items; blk = block index.  Head group of round r, phase ph:
+      // r - ph; heads hgroup * (r - ph) + sub.
+      const int G = p.hgroup;
+      const int ngroups = (p.nheads + G - 1) / G;
+      int r = 0, ph = 0, sub = 0;
       uint32_t blk = 0;
       uint32_t issued = 0;  // bit e: a load was issued on entry e
       uint32_t last_on[kEntries] = {0, 0, 0};
@@ -599,7 +607,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const int e = n % kEntries;
         const uint32_t use = n / kEntries;
         const uint32_t fb = bar(kBarFull, e);
-        if (n >= kEntries && !wait_bar(bar(kBarEmpty, e), (use - 1) & 1, guard)) break;
+        if (!p.early && n >= kEntries && !wait_bar(bar(kBarEmpty, e), (use - 1) & 1, guard))
+          break;
         trace_stamp(p, n, 1, globaltimer());
         const uint32_t w = atomicAdd(ctrl + kCtrlNext, 1u);
         bool ok = w < total && !ld_relaxed(guard.abort);
@@ -608,14 +617,18 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           const uint32_t want = w / kT;
           item = (int)(w % kT);
           while (blk < want) {
-            ++ph;
-            if (ph > (r < P - 1 ? r : P - 1)) {
-              ++r;
-              ph = r - p.nheads + 1 > 0 ? r - p.nheads + 1 : 0;
+            ++sub;
+            if (sub >= G || G * (r - ph) + sub >= p.nheads) {
+              sub = 0;
+              ++ph;
+              if (ph > (r < P - 1 ? r : P - 1)) {
+                ++r;
+                ph = r - ngroups + 1 > 0 ? r - ngroups + 1 : 0;
+              }
             }
             ++blk;
           }
-          head = r - ph;
+          head = G * (r - ph) + sub;
           if (head < 0 || head >= p.nheads) {
             guard.raise(MA_STATUS_BAD_ITEM);
             ok = false;
@@ -631,6 +644,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
             ok = wait_counter(ctrl + kCtrlDone + (head - p.slots) * P + P - 1, (uint32_t)kT,
                               guard);
         }
+        if (p.early && n >= kEntries && !wait_bar(bar(kBarEmpty, e), (use - 1) & 1, guard))
+          break;
         if (!ok) {
           *n_end_s = n;  // items n, n+1, ... do not exist
           mbar_arrive(fb);
@@ -1014,7 +1029,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       mbar_arrive(bar(kBarStaged, e));
       if (row == 0) trace_stamp(p, n, 15, globaltimer());
     }
-  } else if (warp == kStoreWarp) {
+  } else if (warp >= kStoreWarp && warp < kStoreWarp + kStoreWarps) {
     // ===================== TMA stores + publication =====================
     // Per item: wait until its tiles are staged, store them, release the
     // ring entry once the stores have read SMEM, and publish the item once
@@ -1022,7 +1037,9 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
     if (lane == 0) {
       // Publication is immediate: later phases of the head wait for the last
       // item of this one, so any delay here lengthens the phase boundary.
-      for (uint32_t n = 0;; ++n) {
+      // The store warps take alternate items, so one warp's wait for its
+      // writes to complete overlaps the other's stores.
+      for (uint32_t n = warp - kStoreWarp;; n += kStoreWarps) {
         const int e = n % kEntries;
         bool ready = false;
         const uint64_t t0 = globaltimer();
@@ -1148,7 +1165,14 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
       p->dtype == MA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int nheads = s.E * s.H;
   const int P = 2 * s.T;
-  int slots = 2 * s.T + 1;
+  // heads per wavefront phase slot: more heads in flight -> a longer distance
+  // between dependent items (a round is 2T * hgroup * 128 items)
+  int hgroup = 2;  // measured best on B200 (1: 856 us, 2: 785 us, 3: 808 us, 4: 803 us)
+  const char* hg = getenv("MA_TC_GROUP");
+  if (hg) hgroup = atoi(hg);
+  if (hgroup < 1) hgroup = 1;
+  if (hgroup > nheads) hgroup = nheads;
+  int slots = hgroup * (2 * s.T + 1);
   if (slots > nheads) slots = nheads;
   const uint32_t box_blk[4] = {64, kT, 1, 1};
   const uint32_t box_str[5] = {64, 1, kT, 1, 1};
@@ -1216,6 +1240,9 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   tp.T = s.T;
   tp.P = P;
   tp.slots = slots;
+  tp.hgroup = hgroup;
+  const char* ea = getenv("MA_TC_EARLY");  // default on (measured faster with hgroup 2)
+  tp.early = (ea && ea[0] == '0') ? 0 : 1;
   tp.sm_scale = s.sm_scale;
   tp.timeout_ns = 2000000000ull;  // 2 s per bounded wait
   const char* tmo = getenv("MA_WAIT_TIMEOUT_NS");
