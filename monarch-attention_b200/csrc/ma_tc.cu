@@ -209,6 +209,62 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* tm,
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
       : "memory");
 }
+// L2 eviction policies for TMA traffic
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void tma_load_2d_h(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                              uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(bar), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_h(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                              int c2, int c3, uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_5d_h(uint32_t dst, const CUtensorMap* tm, int c0, int c1,
+                                              int c2, int c3, int c4, uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "r"(bar),
+      "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d_h(const CUtensorMap* tm, uint32_t src, int c0, int c1,
+                                               int c2, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint "
+      "[%0, {%2, %3, %4}], [%1], %5;" ::"l"(reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_5d_h(const CUtensorMap* tm, uint32_t src, int c0, int c1,
+                                               int c2, int c3, int c4, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.bulk_group.L2::cache_hint "
+      "[%0, {%2, %3, %4, %5, %6}], [%1], %7;" ::"l"(reinterpret_cast<uint64_t>(tm)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "l"(pol)
+      : "memory");
+}
+// Drop a dead 128-byte line from L2 without writing it back.
+__device__ __forceinline__ void discard_l2(const void* p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* tm, uint32_t src, int c0, int c1,
                                              int c2) {
   asm volatile(
@@ -661,25 +717,31 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
         const uint32_t vdst = sbase + kOffVec + e * 512;
         const size_t vrow = ((size_t)slot * kT + item) * kT;  // cr[slot][m][:] / cl[slot][j][:]
+        // L2 policy: keep what a later phase of this head reads again (q before
+        // the output phase, k before the final R-step); stream last uses and
+        // the single-use intermediates
+        const uint64_t keep = policy_evict_last(), once = policy_evict_first();
         if (kind == KIND_R) {
-          const bool first = ph == 0;
+          const bool first = ph == 0, final_ = ph == P - 2;
           mbar_expect_tx(fb, 2 * kTileBytes + (first ? 0 : 512));
           if (!first) bulk_load(vdst, p.cr + vrow, 512, fb);
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             if (first)
-              tma_load_4d(A + h2 * kHalf, &p.tm_qblk, h2 * 64, item * kT, hh, eb, fb);
+              tma_load_4d_h(A + h2 * kHalf, &p.tm_qblk, h2 * 64, item * kT, hh, eb, fb, keep);
             else
-              tma_load_2d(A + h2 * kHalf, &p.tm_ar, h2 * 64, (slot * kT + item) * kT, fb);
-            tma_load_4d(B + h2 * kHalf, &p.tm_kblk, h2 * 64, item * kT, hh, eb, fb);
+              tma_load_2d_h(A + h2 * kHalf, &p.tm_ar, h2 * 64, (slot * kT + item) * kT, fb, once);
+            tma_load_4d_h(B + h2 * kHalf, &p.tm_kblk, h2 * 64, item * kT, hh, eb, fb,
+                          final_ ? once : keep);
           }
         } else {
           mbar_expect_tx(fb, 2 * kTileBytes + 512);
           bulk_load(vdst, p.cl + vrow, 512, fb);
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
-            tma_load_5d(A + h2 * kHalf, &p.tm_qstr, h2 * 64, item, 0, hh, eb, fb);
-            tma_load_2d(B + h2 * kHalf, &p.tm_al, h2 * 64, (slot * kT + item) * kT, fb);
+            tma_load_5d_h(A + h2 * kHalf, &p.tm_qstr, h2 * 64, item, 0, hh, eb, fb,
+                          kind == KIND_O ? once : keep);
+            tma_load_2d_h(B + h2 * kHalf, &p.tm_al, h2 * 64, (slot * kT + item) * kT, fb, once);
           }
         }
         issued |= 1u << e;
@@ -852,14 +914,26 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       if ((final_ || kind == KIND_O) && row == 0) {
         fence_proxy_async_global();
         const uint32_t xb = bar(kBarX, e);
+        const uint64_t once = policy_evict_first();  // V and y_j: single use
         mbar_expect_tx(xb, kTileBytes);
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
           if (final_)
-            tma_load_4d(A + h2 * kHalf, &p.tm_vblk, h2 * 64, item * kT, hh, eb, xb);
+            tma_load_4d_h(A + h2 * kHalf, &p.tm_vblk, h2 * 64, item * kT, hh, eb, xb, once);
           else
-            tma_load_2d(A + h2 * kHalf, &p.tm_y, h2 * 64, (slot * kT + item) * kT, xb);
+            tma_load_2d_h(A + h2 * kHalf, &p.tm_y, h2 * 64, (slot * kT + item) * kT, xb, once);
         }
+      }
+
+      // The intermediate tiles and vectors this item read have no other
+      // reader: drop them from L2 so their dirty lines are never written back
+      if (kind != KIND_R || ph > 0) {
+        const char* tile = (kind == KIND_R ? p.ar : p.al) + ((size_t)slot * kT + item) * kT * kT * 2;
+        discard_l2(tile + row * 128);
+        discard_l2(tile + (row + 128) * 128);
+        if (row < 4)
+          discard_l2(reinterpret_cast<const char*>((kind == KIND_R ? p.cr : p.cl) +
+                                                   ((size_t)slot * kT + item) * kT) + row * 128);
       }
 
       // The row of S (128 fp32) is streamed out of TMEM in 64-column halves:
@@ -1022,6 +1096,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       } else {
         // z[l*b + j] = (P y_j) / sum (ma_torch.py:60-62)
         stage_row128<BF16>(A, row, tO, scale_out);
+        // y_j has no other reader: drop it from L2 (GEMM2 consumed it)
+        const char* ytile = p.y + ((size_t)slot * kT + item) * kT * kT * 2;
+        discard_l2(ytile + row * 128);
+        discard_l2(ytile + (row + 128) * 128);
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -1064,15 +1142,20 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const bool final_ = kind == KIND_R && ph == P - 2;
         const int eb = head / p.H, hh = head - eb * p.H;
         const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
+        // intermediates are read by the next phase soon: keep them in L2;
+        // the output streams out
+        const uint64_t keep = policy_evict_last(), once = policy_evict_first();
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
           if (kind == KIND_R) {
-            tma_store_3d(&p.tm_al_st, (final_ ? B : A) + h2 * kHalf, h2 * 64, item, slot * kT);
-            if (final_) tma_store_3d(&p.tm_y_st, A + h2 * kHalf, h2 * 64, item, slot * kT);
+            tma_store_3d_h(&p.tm_al_st, (final_ ? B : A) + h2 * kHalf, h2 * 64, item, slot * kT,
+                           keep);
+            if (final_)
+              tma_store_3d_h(&p.tm_y_st, A + h2 * kHalf, h2 * 64, item, slot * kT, keep);
           } else if (kind == KIND_L) {
-            tma_store_3d(&p.tm_ar_st, A + h2 * kHalf, h2 * 64, item, slot * kT);
+            tma_store_3d_h(&p.tm_ar_st, A + h2 * kHalf, h2 * 64, item, slot * kT, keep);
           } else {
-            tma_store_5d(&p.tm_out_st, A + h2 * kHalf, h2 * 64, item, 0, hh, eb);
+            tma_store_5d_h(&p.tm_out_st, A + h2 * kHalf, h2 * 64, item, 0, hh, eb, once);
           }
         }
         bulk_commit();
