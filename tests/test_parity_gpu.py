@@ -204,3 +204,24 @@ def test_missing_library_fails_loudly(monkeypatch, cuda_device):
     q = torch.randn(1, 1, 16, 8, device=cuda_device)
     with pytest.raises(RuntimeError, match="not built"):
         monarch_attention(q, q, q, None, 2, 4, False)
+
+
+# ---------------------------------------------------------------------------
+# float8 e4m3 inputs with per-(e, h) scales: compared with the fp32 oracle run
+# on the dequantised inputs (the quantisation error itself is not counted)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name,shape", [("long4k_e4m3", dict(E=1, H=2)),
+                                        ("long16k_e4m3", dict(E=1, H=1))])
+def test_e4m3_against_dequantised_oracle(name, shape, cuda_device):
+    cfg = CONFIGS[name].with_(**shape)
+    q, k, v, mask, scales = make_inputs(cfg, device=cuda_device)
+    out = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, scales=scales)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert out.dtype == torch.bfloat16
+    deq = [dequantize_e4m3(t, s) for t, s in zip((q, k, v), scales)]
+    ref = oracle_for(*deq, mask, cfg, "f32")
+    got = out.float().cpu().numpy()
+    err = np.abs(got - ref).max()
+    assert np.isfinite(got).all()
+    assert err <= E4M3_TOL * float(np.abs(ref).max()), f"max|err|={err:.3g}"
