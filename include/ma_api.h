@@ -63,7 +63,8 @@ typedef enum {
 typedef enum {
   MA_IMPL_AUTO = 0,
   MA_IMPL_GENERIC = 1, /* any shape/dtype: phase kernels, SIMT fp32 math   */
-  MA_IMPL_TC = 2       /* persistent tcgen05/TMEM kernel (large blocks)     */
+  MA_IMPL_TC = 2,      /* persistent tcgen05/TMEM kernel (large blocks)     */
+  MA_IMPL_SMALL = 3    /* fused per-head mma.sync kernel (b, M <= 32)       */
 } ma_impl_t;
 
 /* Return codes. */
@@ -147,7 +148,7 @@ int ma_fwd(const ma_fwd_params* p, void* stream);
 int ma_fwd_noalloc(const ma_fwd_params* p, void* stream);
 
 /* Which implementation ma_fwd() would run for these params
- * (MA_IMPL_GENERIC or MA_IMPL_TC), or a negative error code. */
+ * (MA_IMPL_GENERIC, MA_IMPL_TC or MA_IMPL_SMALL), or a negative error code. */
 int ma_select_impl(const ma_fwd_params* p);
 
 /* Static description of a return code. */

@@ -18,8 +18,8 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_E4M3 = 0, 1, 2, 3
 # ma_mask_dtype_t
 MASK_NONE, MASK_BOOL, MASK_I32, MASK_I64, MASK_F32, MASK_F16, MASK_BF16 = range(7)
 # ma_impl_t
-IMPL_AUTO, IMPL_GENERIC, IMPL_TC = 0, 1, 2
-IMPL_NAMES = {IMPL_GENERIC: "generic", IMPL_TC: "tc"}
+IMPL_AUTO, IMPL_GENERIC, IMPL_TC, IMPL_SMALL = 0, 1, 2, 3
+IMPL_NAMES = {IMPL_GENERIC: "generic", IMPL_TC: "tc", IMPL_SMALL: "small"}
 
 MA_OK = 0
 MA_ERR_INJECTED = 8

@@ -15,6 +15,10 @@ namespace ma {
 bool generic_supports(const Shape& s);
 cudaError_t run_generic(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
                         cudaStream_t st, int* nlaunch);
+// ma_small.cu
+bool small_supports(const ma_fwd_params* p, const Shape& s);
+cudaError_t run_small(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
+                      cudaStream_t st, int* nlaunch);
 // ma_tc.cu
 bool tc_supports(const ma_fwd_params* p, const Shape& s);
 size_t tc_ctrl_bytes(const Shape& s);
@@ -98,7 +102,7 @@ int validate(const ma_fwd_params* p, bool need_buffers) {
     return fail(MA_ERR_BAD_MASK, "unknown mask dtype");
   if (p->mask_dtype != MA_MASK_NONE && p->mask == nullptr)
     return fail(MA_ERR_BAD_MASK, "mask_dtype set but mask is NULL");
-  if (p->impl < MA_IMPL_AUTO || p->impl > MA_IMPL_TC)
+  if (p->impl < MA_IMPL_AUTO || p->impl > MA_IMPL_SMALL)
     return fail(MA_ERR_BAD_PARAMS, "unknown impl");
   if (!need_buffers) return MA_OK;
   if (!p->q || !p->k || !p->v || !p->out) return fail(MA_ERR_NULL_POINTER, "q/k/v/out is NULL");
@@ -124,6 +128,16 @@ int select_impl(const ma_fwd_params* p, const Shape& s, int* impl) {
   }
   if (p->impl == MA_IMPL_AUTO && tc) {
     *impl = MA_IMPL_TC;
+    return MA_OK;
+  }
+  const bool sm = small_supports(p, s);
+  if (p->impl == MA_IMPL_SMALL) {
+    if (!sm) return fail(MA_ERR_UNSUPPORTED, "the small-block kernel does not support this shape");
+    *impl = MA_IMPL_SMALL;
+    return MA_OK;
+  }
+  if (p->impl == MA_IMPL_AUTO && sm) {
+    *impl = MA_IMPL_SMALL;
     return MA_OK;
   }
   if (!generic_supports(s))
@@ -171,7 +185,9 @@ int ma_fwd(const ma_fwd_params* p, void* stream) {
   if (rc != MA_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int n = 0;
-  cudaError_t err = impl == MA_IMPL_TC ? run_tc(p, s, ws, st, &n) : run_generic(p, s, ws, st, &n);
+  cudaError_t err = impl == MA_IMPL_TC      ? run_tc(p, s, ws, st, &n)
+                    : impl == MA_IMPL_SMALL ? run_small(p, s, ws, st, &n)
+                                            : run_generic(p, s, ws, st, &n);
   if (err != cudaSuccess)
     return fail(MA_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorName(err) + ": " +
                                  cudaGetErrorString(err));

@@ -1,0 +1,518 @@
+// Fused small-block MonarchAttention forward: one CTA runs every phase of one
+// (batch, head) -- the T-1 (R, L) rounds, the final R-step and the output
+// step of ma/ma_torch.py:100-105 -- with __syncthreads between phases and
+// no kernel boundaries.  For block size b <= 32 and number of blocks M <= 32
+// (the ViT, RoBERTa and DiT shapes), D = Dv <= 128, bf16 / fp16, any strides,
+// padding and key-padding mask.
+//
+// Work items of a phase (key blocks m of an R-step, indices j of an L- or
+// output step) are spread over the CTA's warps.  A warp stages its item's
+// operands in shared memory with cp.async (zero-filled padding rows and head
+// dim), computes the 32 x 32 logit tile with mma.sync m16n8k16 (fp32
+// accumulate), the row softmax on the accumulator fragments (quad shuffles),
+// and the output tile with a second mma.sync whose A operand is the
+// probability fragment itself (R / output) or P^T re-read from shared memory
+// (L-step, which contracts over rows).  Intermediates go through a per-head
+// workspace that stays in L2.
+#include <float.h>
+
+#include "ma_common.cuh"
+
+namespace ma {
+namespace small {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRows = 32;  // rows / columns of an item, padded
+
+struct SmallParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int64_t qs[4], ks[4], vs[4], os[4];
+  const void* mask;
+  int64_t ms[2];
+  int mask_dtype;
+  int E, H, N, D, b, M, T, pad_off;
+  float sm_scale;
+  char* al;   // [E*H][b][M][D]
+  char* y;    // [E*H][b][M][D]
+  char* ar;   // [E*H][M][b][D]
+  float* cl;  // [E*H][b][M]
+  float* cr;  // [E*H][M][b]
+};
+
+enum { PH_R = 0, PH_RF = 1, PH_L = 2, PH_O = 3 };
+
+// ---------------------------------------------------------------------------
+// warp-level primitives
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                          uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+template <bool BF16>
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  if (BF16)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  uint32_t r;
+  if (BF16)
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  else
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ bool token_valid(const SmallParams& p, int e, int pidx) {
+  const int n = pidx - p.pad_off;
+  if (n < 0 || n >= p.N) return false;
+  if (p.mask == nullptr) return true;
+  return mask_value(p.mask, p.mask_dtype, (int64_t)e * p.ms[0] + (int64_t)n * p.ms[1]);
+}
+
+// ---------------------------------------------------------------------------
+// one work item, executed by one warp
+// ---------------------------------------------------------------------------
+// Shared-memory tiles of a warp: A, B, X (32 rows x RS 16-bit, RS = DP + 8 so
+// that ldmatrix rows fall in distinct banks) and P^T staging (32 x 40).
+template <typename TI, int DP>
+struct WarpTiles {
+  static constexpr int RS = DP + 8;
+  static constexpr int kTile = kRows * RS;  // elements
+  static constexpr int kPS = 40;            // P staging row stride
+  static constexpr int kBytes = (3 * kTile + kRows * kPS) * 2;
+};
+
+// Copy rows [0, 32) of an operand into a tile; row r comes from `src(r)`
+// (nullptr = zero row).  Only the first D columns are written; the padding
+// columns D..DP stay zero from the kernel prologue.
+template <int DP, typename F>
+__device__ __forceinline__ void stage_rows(uint32_t tile, int D, int lane, F src) {
+  constexpr int RS = DP + 8;
+  const int chunks = D / 8;  // 16-byte chunks per row
+  for (int idx = lane; idx < kRows * chunks; idx += 32) {
+    const int r = idx / chunks, c = idx - r * chunks;
+    const char* s = src(r);
+    cp_async16(tile + (r * RS + c * 8) * 2, s ? s + c * 16 : s, s != nullptr);
+  }
+}
+
+template <int PH, bool BF16, typename TI, int DP>
+__device__ void run_item(const SmallParams& p, int e, int h, int item, int first, uint8_t* wsm,
+                         int lane) {
+  using WT = WarpTiles<TI, DP>;
+  constexpr int RS = WT::RS;
+  constexpr int NK = DP / 16;  // k16 steps over the head dim
+  constexpr int ND = DP / 8;   // n8 tiles over the head dim
+  const int D = p.D, b = p.b, M = p.M;
+  const int eh = e * p.H + h;
+  const uint32_t tA = smem_u32(wsm), tB = tA + WT::kTile * 2, tX = tB + WT::kTile * 2;
+  const uint32_t tP = tX + WT::kTile * 2;
+  const bool rph = PH == PH_R || PH == PH_RF;
+  const int R = rph ? b : M;  // rows of the item
+  const int C = R;            // columns
+  const size_t esz = sizeof(TI);
+
+  auto tok = [&](const void* base, const int64_t* st, int pidx) -> const char* {
+    const int n = pidx - p.pad_off;
+    if (n < 0 || n >= p.N) return nullptr;
+    return reinterpret_cast<const char*>(base) +
+           esz * ((int64_t)e * st[0] + (int64_t)h * st[1] + (int64_t)n * st[2]);
+  };
+  const char* al_h = p.al + (size_t)eh * b * M * D * esz;
+  const char* y_h = p.y + (size_t)eh * b * M * D * esz;
+  const char* ar_h = p.ar + (size_t)eh * M * b * D * esz;
+  const float* cl_h = p.cl + (size_t)eh * b * M;
+  const float* cr_h = p.cr + (size_t)eh * M * b;
+
+  // ---- stage operands ----
+  if (rph) {
+    if (first)
+      stage_rows<DP>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, item * b + r) : nullptr; });
+    else
+      stage_rows<DP>(tA, D, lane, [&](int r) {
+        return r < R ? ar_h + ((size_t)item * b + r) * D * esz : nullptr;
+      });
+    stage_rows<DP>(tB, D, lane, [&](int r) { return r < C ? tok(p.k, p.ks, item * b + r) : nullptr; });
+  } else {
+    stage_rows<DP>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, r * b + item) : nullptr; });
+    stage_rows<DP>(tB, D, lane, [&](int r) {
+      return r < C ? al_h + ((size_t)item * M + r) * D * esz : nullptr;
+    });
+    if (PH == PH_O)
+      stage_rows<DP>(tX, D, lane, [&](int r) {
+        return r < C ? y_h + ((size_t)item * M + r) * D * esz : nullptr;
+      });
+  }
+  cp_async_wait_all();
+  __syncwarp();
+
+  const int g = lane >> 2, t4 = lane & 3;
+
+  // ---- S = A B^T : 32 x 32 tile as acc[mt][nt] ----
+  float acc[2][4][4];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
+#pragma unroll
+  for (int ks = 0; ks < NK; ++ks) {
+    uint32_t a[2][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+      ldsm_x4(tA + ((mt * 16 + (lane & 15)) * RS + ks * 16 + (lane >> 4) * 8) * 2, a[mt][0],
+              a[mt][1], a[mt][2], a[mt][3]);
+#pragma unroll
+    for (int np = 0; np < 2; ++np) {  // pairs of n8 tiles
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(tB + ((np * 16 + (lane & 7) + (lane >> 4) * 8) * RS + ks * 16 + ((lane >> 3) & 1) * 8) * 2,
+              b0, b1, b2, b3);
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        mma16816<BF16>(acc[mt][2 * np], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
+        mma16816<BF16>(acc[mt][2 * np + 1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b2, b3);
+      }
+    }
+  }
+
+  // ---- softmax over the columns of each row ----
+  // fragment element (mt, nt, i): row mt*16 + g + 8*(i>>1), col nt*8 + 2*t4 + (i&1)
+  bool colv[4][2];
+  float colc[4][2];  // per-column term: cl[j][k] (L / out)
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int c = nt * 8 + 2 * t4 + q;
+      colv[nt][q] = c < C && (!rph || token_valid(p, e, item * b + c));
+      colc[nt][q] = (!rph && c < C) ? cl_h[(size_t)item * M + c] : 0.0f;
+    }
+  float row_scale[2][2];  // [mt][half]: 1/den (R) or 1/sum (L / out)
+  float cl_row[2][2];
+#pragma unroll
+  for (int mt = 0; mt < 2; ++mt) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = mt * 16 + g + 8 * hf;
+      float c = 1.0f;
+      if (rph) {
+        const float crj = (first || r >= R) ? 1.0f : cr_h[(size_t)item * b + r];
+        c = p.sm_scale / (crj + kEps);  // ma_torch.py:11-12
+      }
+      // logits (natural units) and row max
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float& x = acc[mt][nt][2 * hf + q];
+          x = rph ? x * c : x - colc[nt][q];
+          if (!colv[nt][q]) x = -INFINITY;
+          mx = fmaxf(mx, x);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      if (rph) mx = fmaxf(mx, kEps);  // clamp(max, min=eps), :14-16
+      float sum = 0.0f, wsum = 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          float& x = acc[mt][nt][2 * hf + q];
+          const float tt = x - mx;
+          const float ev = colv[nt][q] ? __expf(tt) : 0.0f;
+          sum += ev;
+          if (rph && colv[nt][q]) wsum = fmaf(ev, tt, wsum);
+          x = ev;
+        }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if (rph) {
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
+        const float den = sum + kEps;  // :17
+        const float inv = 1.0f / den;
+        cl_row[mt][hf] = inv * wsum - __logf(den) * sum * inv;  // sum r log r, :20
+        row_scale[mt][hf] = inv;
+      } else {
+        cl_row[mt][hf] = 0.0f;
+        row_scale[mt][hf] = 1.0f / sum;
+      }
+      // normalised probabilities (the reference rounds r / l to the input dtype
+      // before its second matmul); L-step: times the query mask of row l (:30)
+      float sc = row_scale[mt][hf];
+      if (PH == PH_L && !(r < R && token_valid(p, e, r * b + item))) sc = 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int q = 0; q < 2; ++q) acc[mt][nt][2 * hf + q] *= sc;
+    }
+  }
+
+  // ---- outputs ----
+  TI* const out_base = nullptr;
+  (void)out_base;
+  if (PH == PH_L) {
+    // cr[k][j] = sum_l P[l][k] (:32): column sums of the fp32 probabilities
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float s = acc[0][nt][q] + acc[0][nt][2 + q] + acc[1][nt][q] + acc[1][nt][2 + q];
+        s += __shfl_xor_sync(0xffffffffu, s, 4);
+        s += __shfl_xor_sync(0xffffffffu, s, 8);
+        s += __shfl_xor_sync(0xffffffffu, s, 16);
+        const int c = nt * 8 + 2 * t4 + q;
+        if (g == 0 && c < C) p.cr[(size_t)eh * M * b + (size_t)c * b + item] = s;
+      }
+    // P (16-bit) -> staging tile Pst[l][k]; ar_j = P^T Q_j reads it transposed
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int r = mt * 16 + g + 8 * hf, c = nt * 8 + 2 * t4;
+          const uint32_t v2 = pack2<BF16>(acc[mt][nt][2 * hf], acc[mt][nt][2 * hf + 1]);
+          asm volatile("st.shared.b32 [%0], %1;" ::"r"(tP + (r * WT::kPS + c) * 2), "r"(v2)
+                       : "memory");
+        }
+    __syncwarp();
+  }
+
+  // O = P X over the item's 32 columns (k16 steps kk = 0, 1); X rows = k
+  //   R: X = K[m] (al), then V[m] (y, final R-step)
+  //   L: A = P^T from staging, X = Q_j (ar)
+  //   out: X = y_j (z)
+  const int nparts = PH == PH_RF ? 2 : 1;
+#pragma unroll 1
+  for (int part = 0; part < nparts; ++part) {
+    if (part == 1) {  // final R-step: V[m] into tile X
+      stage_rows<DP>(tX, D, lane, [&](int r) { return r < C ? tok(p.v, p.vs, item * b + r) : nullptr; });
+      cp_async_wait_all();
+      __syncwarp();
+    }
+    const uint32_t tXo = (rph && part == 0) ? tB : (PH == PH_L ? tA : tX);
+    float o[2][ND][4];
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int nd = 0; nd < ND; ++nd)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[mt][nd][i] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t a[2][4];
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt) {
+        if (PH == PH_L) {
+          // A = P^T: element (k, l) = Pst[l][k]; 8x8 blocks read transposed
+          const int lrow = kk * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int kcol = mt * 16 + ((lane >> 3) & 1) * 8;
+          ldsm_x4_t(tP + (lrow * WT::kPS + kcol) * 2, a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+        } else {
+          a[mt][0] = pack2<BF16>(acc[mt][2 * kk][0], acc[mt][2 * kk][1]);
+          a[mt][1] = pack2<BF16>(acc[mt][2 * kk][2], acc[mt][2 * kk][3]);
+          a[mt][2] = pack2<BF16>(acc[mt][2 * kk + 1][0], acc[mt][2 * kk + 1][1]);
+          a[mt][3] = pack2<BF16>(acc[mt][2 * kk + 1][2], acc[mt][2 * kk + 1][3]);
+        }
+      }
+#pragma unroll
+      for (int np = 0; np < ND / 2; ++np) {
+        uint32_t b0, b1, b2, b3;
+        const int xr = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int xc = np * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(tXo + (xr * RS + xc) * 2, b0, b1, b2, b3);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          mma16816<BF16>(o[mt][2 * np], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
+          mma16816<BF16>(o[mt][2 * np + 1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b2, b3);
+        }
+      }
+    }
+    // store rows: fragment (mt, nd, i) = row mt*16 + g + 8*(i>>1), col nd*8 + 2*t4 + (i&1)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = mt * 16 + g + 8 * hf;
+        if (r >= R) continue;
+        char* dst;
+        float sc = 1.0f;
+        if (rph && part == 0) {  // al[j][m] = sm_scale * (r K[m])  (:21)
+          dst = p.al + ((size_t)eh * b * M + (size_t)r * M + item) * D * esz;
+          sc = p.sm_scale;
+        } else if (rph) {        // y[j][m] = r V[m] (:51)
+          dst = p.y + ((size_t)eh * b * M + (size_t)r * M + item) * D * esz;
+        } else if (PH == PH_L) { // ar[k][j] = sum_l P[l][k] q[l*b+j] (:34)
+          dst = p.ar + ((size_t)eh * M * b + (size_t)r * b + item) * D * esz;
+        } else {                 // z at token l*b + j (:60-62, :106-108)
+          const int n = r * b + item - p.pad_off;
+          if (n < 0 || n >= p.N) continue;
+          dst = reinterpret_cast<char*>(p.out) +
+                esz * ((int64_t)e * p.os[0] + (int64_t)h * p.os[1] + (int64_t)n * p.os[2]);
+        }
+#pragma unroll
+        for (int nd = 0; nd < ND; ++nd) {
+          const int c = nd * 8 + 2 * t4;
+          if (c >= D) continue;
+          const uint32_t v2 =
+              pack2<BF16>(o[mt][nd][2 * hf] * sc, o[mt][nd][2 * hf + 1] * sc);
+          *reinterpret_cast<uint32_t*>(dst + c * esz) = v2;
+        }
+      }
+  }
+  if (rph) {  // cl[j][m] (:20)
+#pragma unroll
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = mt * 16 + g + 8 * hf;
+        if (t4 == 0 && r < R) p.cl[(size_t)eh * b * M + (size_t)r * M + item] = cl_row[mt][hf];
+      }
+  }
+  __syncwarp();
+}
+
+template <bool BF16, typename TI, int DP>
+__global__ void __launch_bounds__(kThreads) ma_small_kernel(const SmallParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  using WT = WarpTiles<TI, DP>;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int eh = blockIdx.x;
+  const int e = eh / p.H, h = eh - e * p.H;
+  uint8_t* wsm = smem + warp * WT::kBytes;
+  // zero the tiles once: padding rows/columns must read as 0
+  for (int i = threadIdx.x; i < kWarps * WT::kBytes / 16; i += kThreads)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+  for (int t = 0; t < p.T; ++t) {
+    const bool final_ = t == p.T - 1;
+    for (int m = warp; m < p.M; m += kWarps) {
+      if (final_)
+        run_item<PH_RF, BF16, TI, DP>(p, e, h, m, t == 0, wsm, lane);
+      else
+        run_item<PH_R, BF16, TI, DP>(p, e, h, m, t == 0, wsm, lane);
+    }
+    __syncthreads();
+    for (int j = warp; j < p.b; j += kWarps) {
+      if (final_)
+        run_item<PH_O, BF16, TI, DP>(p, e, h, j, 0, wsm, lane);
+      else
+        run_item<PH_L, BF16, TI, DP>(p, e, h, j, 0, wsm, lane);
+    }
+    __syncthreads();
+  }
+}
+
+template <bool BF16, typename TI, int DP>
+static cudaError_t launch(const SmallParams& sp, cudaStream_t st) {
+  using WT = WarpTiles<TI, DP>;
+  const size_t smem = (size_t)kWarps * WT::kBytes;
+  auto kfn = ma_small_kernel<BF16, TI, DP>;
+  cudaError_t err =
+      cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  kfn<<<sp.E * sp.H, kThreads, smem, st>>>(sp);
+  return cudaGetLastError();
+}
+
+}  // namespace small
+
+bool small_supports(const ma_fwd_params* p, const Shape& s) {
+  if (p->dtype != MA_DTYPE_BF16 && p->dtype != MA_DTYPE_F16) return false;
+  if (s.b > small::kRows || s.M > small::kRows) return false;
+  if (s.D != s.Dv || s.D % 8 != 0 || s.D > 128) return false;
+  if ((int64_t)s.E * s.H > 2147483647) return false;
+  const int64_t* st[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
+  for (int t = 0; t < 3; ++t) {  // q / k / v rows read with 16-byte copies
+    if (st[t][3] != 1) return false;
+    for (int i = 0; i < 3; ++i)
+      if ((st[t][i] * 2) % 16 != 0) return false;
+  }
+  if (st[3][3] != 1 || (st[3][2] * 2) % 4 != 0) return false;
+  const void* ptrs[3] = {p->q, p->k, p->v};
+  for (int i = 0; i < 3; ++i)
+    if (ptrs[i] && (reinterpret_cast<uintptr_t>(ptrs[i]) & 15)) return false;
+  if (p->out && (reinterpret_cast<uintptr_t>(p->out) & 3)) return false;
+  return true;
+}
+
+cudaError_t run_small(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
+                      cudaStream_t st, int* nlaunch) {
+  small::SmallParams sp{};
+  sp.q = p->q; sp.k = p->k; sp.v = p->v; sp.out = p->out;
+  for (int i = 0; i < 4; ++i) {
+    sp.qs[i] = p->q_stride[i]; sp.ks[i] = p->k_stride[i];
+    sp.vs[i] = p->v_stride[i]; sp.os[i] = p->o_stride[i];
+  }
+  sp.mask = p->mask_dtype == MA_MASK_NONE ? nullptr : p->mask;
+  sp.ms[0] = p->mask_stride[0]; sp.ms[1] = p->mask_stride[1];
+  sp.mask_dtype = p->mask_dtype;
+  sp.E = s.E; sp.H = s.H; sp.N = s.N; sp.D = s.D; sp.b = s.b; sp.M = s.M; sp.T = s.T;
+  sp.pad_off = s.pad_off; sp.sm_scale = s.sm_scale;
+  char* w = reinterpret_cast<char*>(p->workspace);
+  sp.al = w + ws.al; sp.y = w + ws.y; sp.ar = w + ws.ar;
+  sp.cl = reinterpret_cast<float*>(w + ws.cl);
+  sp.cr = reinterpret_cast<float*>(w + ws.cr);
+  const bool bf = p->dtype == MA_DTYPE_BF16;
+  const int dp = (s.D + 15) / 16 * 16;
+  cudaError_t err;
+#define MA_SMALL_CASE(DPV)                                                              \
+  case DPV:                                                                             \
+    err = bf ? small::launch<true, __nv_bfloat16, DPV>(sp, st)                          \
+             : small::launch<false, __half, DPV>(sp, st);                               \
+    break;
+  switch (dp) {
+    MA_SMALL_CASE(16)
+    MA_SMALL_CASE(32)
+    MA_SMALL_CASE(48)
+    MA_SMALL_CASE(64)
+    MA_SMALL_CASE(80)
+    MA_SMALL_CASE(96)
+    MA_SMALL_CASE(112)
+    MA_SMALL_CASE(128)
+    default: return cudaErrorInvalidValue;
+  }
+#undef MA_SMALL_CASE
+  if (err == cudaSuccess) *nlaunch += 1;
+  return err;
+}
+
+}  // namespace ma

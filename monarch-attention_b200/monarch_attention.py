@@ -58,6 +58,7 @@ _IMPL_ARG = {
     "triton": _lib.IMPL_AUTO,
     "generic": _lib.IMPL_GENERIC,
     "tc": _lib.IMPL_TC,
+    "small": _lib.IMPL_SMALL,
 }
 
 
@@ -210,7 +211,8 @@ def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None,
 
 def selected_impl(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int, B: int,
                   pre_pad: bool, impl=None) -> str:
-    """Name of the kernel family ``monarch_attention`` would run ("generic" / "tc")."""
+    """Name of the kernel family ``monarch_attention`` would run
+    ("generic" / "tc" / "small")."""
     lib = _lib.load()
     out = torch.empty((1,), device=q.device)
     p, _keep = build_params(q, k, v, out, attn_mask, T, B, pre_pad, _impl_code(impl))
@@ -228,7 +230,7 @@ class MonarchAttention(nn.Module):
     """MonarchAttention (ma/monarch_attention.py:17-70) on B200 CUDA kernels.
 
     ``impl``: None / "auto" (default) picks the fastest kernel for the shape;
-    "generic" or "tc" force a kernel family; the reference's "torch" and
+    "generic", "tc" or "small" force a kernel family; the reference's "torch" and
     "triton" are accepted and mean "auto".  The MA_IMPL environment variable
     overrides it (for tests).
     """

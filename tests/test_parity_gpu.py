@@ -43,12 +43,16 @@ def check_status(dev):
 # ---------------------------------------------------------------------------
 # golden fixtures (outputs of the reference itself)
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("impl", ["auto", "generic"])
+@pytest.mark.parametrize("impl", ["auto", "generic", "small"])
 @pytest.mark.parametrize("path", golden_paths(), ids=lambda p: os.path.basename(p)[:-4])
 def test_golden(path, impl, cuda_device):
     c = load_case(path)
     m = c["meta"]
     dt = m["dtype"]
+    if impl == "small" and not (dt in ("bf16", "f16") and m["B"] <= 32
+                                and -(-m["N"] // m["B"]) <= 32 and m["D"] == m["Dv"]
+                                and m["D"] % 8 == 0):
+        pytest.skip("outside the small-block kernel's shapes")
     q, k, v = (to_dev(c[n], dt, cuda_device) for n in ("q", "k", "v"))
     mask = None if "mask" not in c else torch.from_numpy(c["mask"]).to(cuda_device)
     out = monarch_attention(q, k, v, mask, m["T"], m["B"], m["pre_pad"], impl=impl)
@@ -81,10 +85,12 @@ def oracle_for(q, k, v, mask, cfg, dt):
     return monarch_attention_oracle_heads(qn, kn, vn, mn, cfg.T, cfg.B, cfg.pre_pad, dt)
 
 
-@pytest.mark.parametrize("impl", ["auto", "generic"])
+@pytest.mark.parametrize("impl", ["auto", "generic", "small"])
 @pytest.mark.parametrize("name", list(SMALL))
 def test_config_small(name, impl, cuda_device):
     cfg = CONFIGS[name].with_(**SMALL[name])
+    if impl == "small" and (cfg.dtype == "f32" or cfg.B > 32 or cfg.M > 32):
+        pytest.skip("outside the small-block kernel's shapes")
     q, k, v, mask, _ = make_inputs(cfg, device="cpu")
     out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
                             None if mask is None else mask.to(cuda_device),
