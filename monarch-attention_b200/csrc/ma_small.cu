@@ -56,6 +56,11 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
                "r"(valid ? 16 : 0)
                : "memory");
 }
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src),
+               "r"(valid ? 4 : 0)
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }
@@ -103,45 +108,61 @@ __device__ __forceinline__ bool token_valid(const SmallParams& p, int e, int pid
   if (p.mask == nullptr) return true;
   return mask_value(p.mask, p.mask_dtype, (int64_t)e * p.ms[0] + (int64_t)n * p.ms[1]);
 }
+// validity of padded token pidx from the CTA's bitmap (built in the prologue)
+__device__ __forceinline__ bool valid_bit(const uint32_t* bits, int pidx) {
+  return (bits[pidx >> 5] >> (pidx & 31)) & 1u;
+}
 
 // ---------------------------------------------------------------------------
 // one work item, executed by one warp
 // ---------------------------------------------------------------------------
 // Shared-memory tiles of a warp: A, B, X (32 rows x RS 16-bit, RS = DP + 8 so
 // that ldmatrix rows fall in distinct banks) and P^T staging (32 x 40).
-template <typename TI, int DP>
+template <typename TI, int DP, int ROWS>
 struct WarpTiles {
   static constexpr int RS = DP + 8;
-  static constexpr int kTile = kRows * RS;  // elements
-  static constexpr int kPS = 40;            // P staging row stride
-  static constexpr int kBytes = (3 * kTile + kRows * kPS) * 2;
+  static constexpr int kTile = ROWS * RS;   // elements
+  static constexpr int kPS = ROWS + 8;      // P staging row stride (in tile X: L items have no X)
+  static constexpr int kVec = ROWS * 4;     // cr / cl vector of the item (fp32)
+  static constexpr int kTileX = ROWS * (RS > kPS ? RS : kPS);  // tile X doubles as P staging
+  static constexpr int kBytes = (2 * kTile + kTileX) * 2 + kVec;
+  static constexpr int kMaxTokens = ROWS * ROWS;  // padded sequence length N_p
+  static constexpr int kBitmapBytes = kMaxTokens / 8 < 16 ? 16 : kMaxTokens / 8;
 };
 
-// Copy rows [0, 32) of an operand into a tile; row r comes from `src(r)`
+// Copy rows [0, ROWS) of an operand into a tile; row r comes from `src(r)`
 // (nullptr = zero row).  Only the first D columns are written; the padding
 // columns D..DP stay zero from the kernel prologue.
-template <int DP, typename F>
+template <int DP, int ROWS, typename F>
 __device__ __forceinline__ void stage_rows(uint32_t tile, int D, int lane, F src) {
   constexpr int RS = DP + 8;
-  const int chunks = D / 8;  // 16-byte chunks per row
-  for (int idx = lane; idx < kRows * chunks; idx += 32) {
-    const int r = idx / chunks, c = idx - r * chunks;
-    const char* s = src(r);
-    cp_async16(tile + (r * RS + c * 8) * 2, s ? s + c * 16 : s, s != nullptr);
+  constexpr int CH = DP / 8;  // 16-byte chunks per padded row
+  const int chunks = D / 8;
+#pragma unroll
+  for (int idx = lane; idx < ROWS * CH; idx += 32) {
+    const int r = idx / CH, c = idx - r * CH;
+    if (c < chunks) {
+      const char* s = src(r);
+      cp_async16(tile + (r * RS + c * 8) * 2, s ? s + c * 16 : s, s != nullptr);
+    }
   }
 }
 
-template <int PH, bool BF16, typename TI, int DP>
+template <int PH, bool BF16, typename TI, int DP, int ROWS>
 __device__ void run_item(const SmallParams& p, int e, int h, int item, int first, uint8_t* wsm,
-                         int lane) {
-  using WT = WarpTiles<TI, DP>;
+                         const uint32_t* vbits, int lane) {
+  using WT = WarpTiles<TI, DP, ROWS>;
+  constexpr int MT = ROWS / 16;  // m16 tiles of the item
+  constexpr int NT = ROWS / 8;   // n8 tiles of its columns
   constexpr int RS = WT::RS;
   constexpr int NK = DP / 16;  // k16 steps over the head dim
   constexpr int ND = DP / 8;   // n8 tiles over the head dim
   const int D = p.D, b = p.b, M = p.M;
   const int eh = e * p.H + h;
   const uint32_t tA = smem_u32(wsm), tB = tA + WT::kTile * 2, tX = tB + WT::kTile * 2;
-  const uint32_t tP = tX + WT::kTile * 2;
+  const uint32_t tP = tX;                        // P staging of L items
+  const uint32_t tV = tX + WT::kTileX * 2;       // cr[m][:] (R) or cl[j][:] (L / out)
+  const float* vec = reinterpret_cast<const float*>(wsm + (tV - tA));
   const bool rph = PH == PH_R || PH == PH_RF;
   const int R = rph ? b : M;  // rows of the item
   const int C = R;            // columns
@@ -162,86 +183,95 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
   // ---- stage operands ----
   if (rph) {
     if (first)
-      stage_rows<DP>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, item * b + r) : nullptr; });
+      stage_rows<DP, ROWS>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, item * b + r) : nullptr; });
     else
-      stage_rows<DP>(tA, D, lane, [&](int r) {
+      stage_rows<DP, ROWS>(tA, D, lane, [&](int r) {
         return r < R ? ar_h + ((size_t)item * b + r) * D * esz : nullptr;
       });
-    stage_rows<DP>(tB, D, lane, [&](int r) { return r < C ? tok(p.k, p.ks, item * b + r) : nullptr; });
+    stage_rows<DP, ROWS>(tB, D, lane, [&](int r) { return r < C ? tok(p.k, p.ks, item * b + r) : nullptr; });
   } else {
-    stage_rows<DP>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, r * b + item) : nullptr; });
-    stage_rows<DP>(tB, D, lane, [&](int r) {
+    stage_rows<DP, ROWS>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, r * b + item) : nullptr; });
+    stage_rows<DP, ROWS>(tB, D, lane, [&](int r) {
       return r < C ? al_h + ((size_t)item * M + r) * D * esz : nullptr;
     });
     if (PH == PH_O)
-      stage_rows<DP>(tX, D, lane, [&](int r) {
+      stage_rows<DP, ROWS>(tX, D, lane, [&](int r) {
         return r < C ? y_h + ((size_t)item * M + r) * D * esz : nullptr;
       });
+  }
+  if (!(rph && first)) {  // the item's cr / cl vector (one fp32 per lane, 0 beyond it)
+    const float* vsrc = rph ? cr_h + (size_t)item * b : cl_h + (size_t)item * M;
+    if (lane < ROWS) {
+      const bool ok = lane < (rph ? b : M);
+      cp_async4(tV + lane * 4, ok ? vsrc + lane : vsrc, ok);
+    }
   }
   cp_async_wait_all();
   __syncwarp();
 
+  // The item is processed one 16-row tile (mt) at a time: S row tile ->
+  // softmax -> (R / out) output row tile; the L-step first puts the
+  // probabilities of every row tile in the staging tile, then computes its
+  // output (rows k of P^T Q_j) one 16-row tile at a time.
   const int g = lane >> 2, t4 = lane & 3;
-
-  // ---- S = A B^T : 32 x 32 tile as acc[mt][nt] ----
-  float acc[2][4][4];
+  bool colv[NT][2];
+  float colc[NT][2];  // per-column term: cl[j][k] (L / out)
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[mt][nt][i] = 0.0f;
-#pragma unroll
-  for (int ks = 0; ks < NK; ++ks) {
-    uint32_t a[2][4];
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
-      ldsm_x4(tA + ((mt * 16 + (lane & 15)) * RS + ks * 16 + (lane >> 4) * 8) * 2, a[mt][0],
-              a[mt][1], a[mt][2], a[mt][3]);
-#pragma unroll
-    for (int np = 0; np < 2; ++np) {  // pairs of n8 tiles
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(tB + ((np * 16 + (lane & 7) + (lane >> 4) * 8) * RS + ks * 16 + ((lane >> 3) & 1) * 8) * 2,
-              b0, b1, b2, b3);
-#pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        mma16816<BF16>(acc[mt][2 * np], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
-        mma16816<BF16>(acc[mt][2 * np + 1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b2, b3);
-      }
-    }
-  }
-
-  // ---- softmax over the columns of each row ----
-  // fragment element (mt, nt, i): row mt*16 + g + 8*(i>>1), col nt*8 + 2*t4 + (i&1)
-  bool colv[4][2];
-  float colc[4][2];  // per-column term: cl[j][k] (L / out)
-#pragma unroll
-  for (int nt = 0; nt < 4; ++nt)
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int c = nt * 8 + 2 * t4 + q;
-      colv[nt][q] = c < C && (!rph || token_valid(p, e, item * b + c));
-      colc[nt][q] = (!rph && c < C) ? cl_h[(size_t)item * M + c] : 0.0f;
+      colv[nt][q] = c < C && (!rph || valid_bit(vbits, item * b + c));
+      colc[nt][q] = (!rph && c < C) ? vec[c] : 0.0f;
     }
-  float row_scale[2][2];  // [mt][half]: 1/den (R) or 1/sum (L / out)
-  float cl_row[2][2];
+  float colsum[NT][2];  // L-step: column sums of P over the rows (cr)
 #pragma unroll
-  for (int mt = 0; mt < 2; ++mt) {
+  for (int nt = 0; nt < NT; ++nt) colsum[nt][0] = colsum[nt][1] = 0.0f;
+  const int nparts = PH == PH_RF ? 2 : 1;
+  if (PH == PH_RF) {  // V[m] for the second output part, staged with the item
+    stage_rows<DP, ROWS>(tX, D, lane, [&](int r) { return r < C ? tok(p.v, p.vs, item * b + r) : nullptr; });
+    cp_async_wait_all();
+    __syncwarp();
+  }
+
+#pragma unroll 1
+  for (int mt = 0; mt < MT; ++mt) {
+    // ---- S row tile = A[mt] B^T : 16 x ROWS ----
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[nt][i] = 0.0f;
+#pragma unroll
+    for (int ks = 0; ks < NK; ++ks) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(tA + ((mt * 16 + (lane & 15)) * RS + ks * 16 + (lane >> 4) * 8) * 2, a0, a1, a2, a3);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {  // pairs of n8 tiles
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(tB + ((np * 16 + (lane & 7) + (lane >> 4) * 8) * RS + ks * 16 + ((lane >> 3) & 1) * 8) * 2,
+                b0, b1, b2, b3);
+        mma16816<BF16>(acc[2 * np], a0, a1, a2, a3, b0, b1);
+        mma16816<BF16>(acc[2 * np + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // ---- softmax over the columns of each row ----
+    // fragment element (nt, i): row mt*16 + g + 8*(i>>1), col nt*8 + 2*t4 + (i&1)
+    float row_scale[2], cl_row[2];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       const int r = mt * 16 + g + 8 * hf;
       float c = 1.0f;
       if (rph) {
-        const float crj = (first || r >= R) ? 1.0f : cr_h[(size_t)item * b + r];
+        const float crj = (first || r >= R) ? 1.0f : vec[r];
         c = p.sm_scale / (crj + kEps);  // ma_torch.py:11-12
       }
-      // logits (natural units) and row max
       float mx = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          float& x = acc[mt][nt][2 * hf + q];
+          float& x = acc[nt][2 * hf + q];
           x = rph ? x * c : x - colc[nt][q];
           if (!colv[nt][q]) x = -INFINITY;
           mx = fmaxf(mx, x);
@@ -251,10 +281,10 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
       if (rph) mx = fmaxf(mx, kEps);  // clamp(max, min=eps), :14-16
       float sum = 0.0f, wsum = 0.0f;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          float& x = acc[mt][nt][2 * hf + q];
+          float& x = acc[nt][2 * hf + q];
           const float tt = x - mx;
           const float ev = colv[nt][q] ? __expf(tt) : 0.0f;
           sum += ev;
@@ -268,107 +298,72 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
         wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
         const float den = sum + kEps;  // :17
         const float inv = 1.0f / den;
-        cl_row[mt][hf] = inv * wsum - __logf(den) * sum * inv;  // sum r log r, :20
-        row_scale[mt][hf] = inv;
+        cl_row[hf] = inv * wsum - __logf(den) * sum * inv;  // sum r log r, :20
+        row_scale[hf] = inv;
       } else {
-        cl_row[mt][hf] = 0.0f;
-        row_scale[mt][hf] = 1.0f / sum;
+        cl_row[hf] = 0.0f;
+        row_scale[hf] = 1.0f / sum;
       }
       // normalised probabilities (the reference rounds r / l to the input dtype
       // before its second matmul); L-step: times the query mask of row l (:30)
-      float sc = row_scale[mt][hf];
-      if (PH == PH_L && !(r < R && token_valid(p, e, r * b + item))) sc = 0.0f;
+      float sc = row_scale[hf];
+      if (PH == PH_L && !(r < R && valid_bit(vbits, r * b + item))) sc = 0.0f;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int q = 0; q < 2; ++q) acc[mt][nt][2 * hf + q] *= sc;
+        for (int q = 0; q < 2; ++q) acc[nt][2 * hf + q] *= sc;
     }
-  }
-
-  // ---- outputs ----
-  TI* const out_base = nullptr;
-  (void)out_base;
-  if (PH == PH_L) {
-    // cr[k][j] = sum_l P[l][k] (:32): column sums of the fp32 probabilities
+    if (rph) {  // cl[j][m] (:20)
 #pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        float s = acc[0][nt][q] + acc[0][nt][2 + q] + acc[1][nt][q] + acc[1][nt][2 + q];
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        s += __shfl_xor_sync(0xffffffffu, s, 8);
-        s += __shfl_xor_sync(0xffffffffu, s, 16);
-        const int c = nt * 8 + 2 * t4 + q;
-        if (g == 0 && c < C) p.cr[(size_t)eh * M * b + (size_t)c * b + item] = s;
+      for (int hf = 0; hf < 2; ++hf) {
+        const int r = mt * 16 + g + 8 * hf;
+        if (t4 == 0 && r < R) p.cl[(size_t)eh * b * M + (size_t)r * M + item] = cl_row[hf];
       }
-    // P (16-bit) -> staging tile Pst[l][k]; ar_j = P^T Q_j reads it transposed
+    }
+
+    if (PH == PH_L) {
+      // cr partial sums and P (16-bit) -> staging tile Pst[l][k]
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+        for (int q = 0; q < 2; ++q) colsum[nt][q] += acc[nt][q] + acc[nt][2 + q];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           const int r = mt * 16 + g + 8 * hf, c = nt * 8 + 2 * t4;
-          const uint32_t v2 = pack2<BF16>(acc[mt][nt][2 * hf], acc[mt][nt][2 * hf + 1]);
+          const uint32_t v2 = pack2<BF16>(acc[nt][2 * hf], acc[nt][2 * hf + 1]);
           asm volatile("st.shared.b32 [%0], %1;" ::"r"(tP + (r * WT::kPS + c) * 2), "r"(v2)
                        : "memory");
         }
-    __syncwarp();
-  }
-
-  // O = P X over the item's 32 columns (k16 steps kk = 0, 1); X rows = k
-  //   R: X = K[m] (al), then V[m] (y, final R-step)
-  //   L: A = P^T from staging, X = Q_j (ar)
-  //   out: X = y_j (z)
-  const int nparts = PH == PH_RF ? 2 : 1;
-#pragma unroll 1
-  for (int part = 0; part < nparts; ++part) {
-    if (part == 1) {  // final R-step: V[m] into tile X
-      stage_rows<DP>(tX, D, lane, [&](int r) { return r < C ? tok(p.v, p.vs, item * b + r) : nullptr; });
-      cp_async_wait_all();
-      __syncwarp();
+      continue;
     }
-    const uint32_t tXo = (rph && part == 0) ? tB : (PH == PH_L ? tA : tX);
-    float o[2][ND][4];
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+
+    // ---- R / out: output row tile O = P X over the item's ROWS columns ----
+#pragma unroll 1
+    for (int part = 0; part < nparts; ++part) {
+      const uint32_t tXo = (rph && part == 0) ? tB : tX;  // K[m] / V[m] / y_j
+      float o[ND][4];
 #pragma unroll
       for (int nd = 0; nd < ND; ++nd)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) o[mt][nd][i] = 0.0f;
+        for (int i = 0; i < 4; ++i) o[nd][i] = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      uint32_t a[2][4];
+      for (int kk = 0; kk < ROWS / 16; ++kk) {
+        const uint32_t a0 = pack2<BF16>(acc[2 * kk][0], acc[2 * kk][1]);
+        const uint32_t a1 = pack2<BF16>(acc[2 * kk][2], acc[2 * kk][3]);
+        const uint32_t a2 = pack2<BF16>(acc[2 * kk + 1][0], acc[2 * kk + 1][1]);
+        const uint32_t a3 = pack2<BF16>(acc[2 * kk + 1][2], acc[2 * kk + 1][3]);
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt) {
-        if (PH == PH_L) {
-          // A = P^T: element (k, l) = Pst[l][k]; 8x8 blocks read transposed
-          const int lrow = kk * 16 + (lane & 7) + ((lane >> 4) << 3);
-          const int kcol = mt * 16 + ((lane >> 3) & 1) * 8;
-          ldsm_x4_t(tP + (lrow * WT::kPS + kcol) * 2, a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
-        } else {
-          a[mt][0] = pack2<BF16>(acc[mt][2 * kk][0], acc[mt][2 * kk][1]);
-          a[mt][1] = pack2<BF16>(acc[mt][2 * kk][2], acc[mt][2 * kk][3]);
-          a[mt][2] = pack2<BF16>(acc[mt][2 * kk + 1][0], acc[mt][2 * kk + 1][1]);
-          a[mt][3] = pack2<BF16>(acc[mt][2 * kk + 1][2], acc[mt][2 * kk + 1][3]);
+        for (int np = 0; np < ND / 2; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int xr = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int xc = np * 16 + (lane >> 4) * 8;
+          ldsm_x4_t(tXo + (xr * RS + xc) * 2, b0, b1, b2, b3);
+          mma16816<BF16>(o[2 * np], a0, a1, a2, a3, b0, b1);
+          mma16816<BF16>(o[2 * np + 1], a0, a1, a2, a3, b2, b3);
         }
       }
-#pragma unroll
-      for (int np = 0; np < ND / 2; ++np) {
-        uint32_t b0, b1, b2, b3;
-        const int xr = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int xc = np * 16 + (lane >> 4) * 8;
-        ldsm_x4_t(tXo + (xr * RS + xc) * 2, b0, b1, b2, b3);
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-          mma16816<BF16>(o[mt][2 * np], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b0, b1);
-          mma16816<BF16>(o[mt][2 * np + 1], a[mt][0], a[mt][1], a[mt][2], a[mt][3], b2, b3);
-        }
-      }
-    }
-    // store rows: fragment (mt, nd, i) = row mt*16 + g + 8*(i>>1), col nd*8 + 2*t4 + (i&1)
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int r = mt * 16 + g + 8 * hf;
@@ -380,8 +375,6 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
           sc = p.sm_scale;
         } else if (rph) {        // y[j][m] = r V[m] (:51)
           dst = p.y + ((size_t)eh * b * M + (size_t)r * M + item) * D * esz;
-        } else if (PH == PH_L) { // ar[k][j] = sum_l P[l][k] q[l*b+j] (:34)
-          dst = p.ar + ((size_t)eh * M * b + (size_t)r * b + item) * D * esz;
         } else {                 // z at token l*b + j (:60-62, :106-108)
           const int n = r * b + item - p.pad_off;
           if (n < 0 || n >= p.N) continue;
@@ -392,60 +385,116 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
         for (int nd = 0; nd < ND; ++nd) {
           const int c = nd * 8 + 2 * t4;
           if (c >= D) continue;
-          const uint32_t v2 =
-              pack2<BF16>(o[mt][nd][2 * hf] * sc, o[mt][nd][2 * hf + 1] * sc);
-          *reinterpret_cast<uint32_t*>(dst + c * esz) = v2;
+          *reinterpret_cast<uint32_t*>(dst + c * esz) =
+              pack2<BF16>(o[nd][2 * hf] * sc, o[nd][2 * hf + 1] * sc);
         }
       }
+    }
   }
-  if (rph) {  // cl[j][m] (:20)
+
+  if (PH == PH_L) {
+    // cr[k][j] = sum_l P[l][k] (:32)
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        float sm = colsum[nt][q];
+        sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 8);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 16);
+        const int c = nt * 8 + 2 * t4 + q;
+        if (g == 0 && c < C) p.cr[(size_t)eh * M * b + (size_t)c * b + item] = sm;
+      }
+    __syncwarp();
+    // ar[k][j] = sum_l P[l][k] q[l*b+j] (:34): A = P^T read transposed from the
+    // staging tile, B = Q_j (tile A), one 16-row tile of k at a time
+#pragma unroll 1
+    for (int mt = 0; mt < MT; ++mt) {
+      float o[ND][4];
+#pragma unroll
+      for (int nd = 0; nd < ND; ++nd)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[nd][i] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < ROWS / 16; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        const int lrow = kk * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int kcol = mt * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4_t(tP + (lrow * WT::kPS + kcol) * 2, a0, a1, a2, a3);
+#pragma unroll
+        for (int np = 0; np < ND / 2; ++np) {
+          uint32_t b0, b1, b2, b3;
+          const int xr = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int xc = np * 16 + (lane >> 4) * 8;
+          ldsm_x4_t(tA + (xr * RS + xc) * 2, b0, b1, b2, b3);
+          mma16816<BF16>(o[2 * np], a0, a1, a2, a3, b0, b1);
+          mma16816<BF16>(o[2 * np + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
-        const int r = mt * 16 + g + 8 * hf;
-        if (t4 == 0 && r < R) p.cl[(size_t)eh * b * M + (size_t)r * M + item] = cl_row[mt][hf];
+        const int r = mt * 16 + g + 8 * hf;  // k
+        if (r >= R) continue;
+        char* dst = p.ar + ((size_t)eh * M * b + (size_t)r * b + item) * D * esz;
+#pragma unroll
+        for (int nd = 0; nd < ND; ++nd) {
+          const int c = nd * 8 + 2 * t4;
+          if (c >= D) continue;
+          *reinterpret_cast<uint32_t*>(dst + c * esz) = pack2<BF16>(o[nd][2 * hf], o[nd][2 * hf + 1]);
+        }
       }
+    }
   }
   __syncwarp();
 }
 
-template <bool BF16, typename TI, int DP>
-__global__ void __launch_bounds__(kThreads) ma_small_kernel(const SmallParams p) {
+template <bool BF16, typename TI, int DP, int ROWS>
+__global__ void __launch_bounds__(kThreads, ROWS == 16 ? 4 : 3) ma_small_kernel(const SmallParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
-  using WT = WarpTiles<TI, DP>;
+  using WT = WarpTiles<TI, DP, ROWS>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int eh = blockIdx.x;
   const int e = eh / p.H, h = eh - e * p.H;
   uint8_t* wsm = smem + warp * WT::kBytes;
+  uint32_t* vbits = reinterpret_cast<uint32_t*>(smem + kWarps * WT::kBytes);
   // zero the tiles once: padding rows/columns must read as 0
   for (int i = threadIdx.x; i < kWarps * WT::kBytes / 16; i += kThreads)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  // token validity of the padded sequence (pad positions and the mask row)
+  const int Np = p.M * p.b;
+  for (int w = threadIdx.x; w < (WT::kMaxTokens + 31) / 32; w += kThreads) {
+    uint32_t bits = 0;
+    for (int i = 0; i < 32; ++i) {
+      const int pidx = w * 32 + i;
+      if (pidx < Np && token_valid(p, e, pidx)) bits |= 1u << i;
+    }
+    vbits[w] = bits;
+  }
   __syncthreads();
   for (int t = 0; t < p.T; ++t) {
     const bool final_ = t == p.T - 1;
     for (int m = warp; m < p.M; m += kWarps) {
       if (final_)
-        run_item<PH_RF, BF16, TI, DP>(p, e, h, m, t == 0, wsm, lane);
+        run_item<PH_RF, BF16, TI, DP, ROWS>(p, e, h, m, t == 0, wsm, vbits, lane);
       else
-        run_item<PH_R, BF16, TI, DP>(p, e, h, m, t == 0, wsm, lane);
+        run_item<PH_R, BF16, TI, DP, ROWS>(p, e, h, m, t == 0, wsm, vbits, lane);
     }
     __syncthreads();
     for (int j = warp; j < p.b; j += kWarps) {
       if (final_)
-        run_item<PH_O, BF16, TI, DP>(p, e, h, j, 0, wsm, lane);
+        run_item<PH_O, BF16, TI, DP, ROWS>(p, e, h, j, 0, wsm, vbits, lane);
       else
-        run_item<PH_L, BF16, TI, DP>(p, e, h, j, 0, wsm, lane);
+        run_item<PH_L, BF16, TI, DP, ROWS>(p, e, h, j, 0, wsm, vbits, lane);
     }
     __syncthreads();
   }
 }
 
-template <bool BF16, typename TI, int DP>
+template <bool BF16, typename TI, int DP, int ROWS>
 static cudaError_t launch(const SmallParams& sp, cudaStream_t st) {
-  using WT = WarpTiles<TI, DP>;
-  const size_t smem = (size_t)kWarps * WT::kBytes;
-  auto kfn = ma_small_kernel<BF16, TI, DP>;
+  using WT = WarpTiles<TI, DP, ROWS>;
+  const size_t smem = (size_t)kWarps * WT::kBytes + WT::kBitmapBytes;
+  auto kfn = ma_small_kernel<BF16, TI, DP, ROWS>;
   cudaError_t err =
       cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
@@ -494,10 +543,15 @@ cudaError_t run_small(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
   const bool bf = p->dtype == MA_DTYPE_BF16;
   const int dp = (s.D + 15) / 16 * 16;
   cudaError_t err;
+  const bool r16 = s.b <= 16 && s.M <= 16;
 #define MA_SMALL_CASE(DPV)                                                              \
   case DPV:                                                                             \
-    err = bf ? small::launch<true, __nv_bfloat16, DPV>(sp, st)                          \
-             : small::launch<false, __half, DPV>(sp, st);                               \
+    if (r16)                                                                            \
+      err = bf ? small::launch<true, __nv_bfloat16, DPV, 16>(sp, st)                    \
+               : small::launch<false, __half, DPV, 16>(sp, st);                         \
+    else                                                                                \
+      err = bf ? small::launch<true, __nv_bfloat16, DPV, 32>(sp, st)                    \
+               : small::launch<false, __half, DPV, 32>(sp, st);                         \
     break;
   switch (dp) {
     MA_SMALL_CASE(16)
