@@ -19,6 +19,9 @@ cudaError_t run_generic(const ma_fwd_params* p, const Shape& s, const WsLayout& 
 bool small_supports(const ma_fwd_params* p, const Shape& s);
 cudaError_t run_small(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
                       cudaStream_t st, int* nlaunch);
+// ma_convert.cu
+cudaError_t run_e4m3_to_bf16(const ma_fwd_params* p, const Shape& s, void* dq, void* dk, void* dv,
+                             cudaStream_t st, int* nlaunch);
 // ma_tc.cu
 bool tc_supports(const ma_fwd_params* p, const Shape& s);
 size_t tc_ctrl_bytes(const Shape& s);
@@ -61,7 +64,8 @@ Shape make_shape(const ma_fwd_params* p) {
   return s;
 }
 
-WsLayout make_layout(const Shape& s, int dtype) {
+// conv: reserve bf16 copies of e4m3 q / k / v (tensor-core kernels)
+WsLayout make_layout(const Shape& s, int dtype, bool conv) {
   WsLayout w{};
   // intermediates are kept in the input precision; e4m3 inputs use bf16
   w.store_bytes = dtype == MA_DTYPE_F32 ? 4 : 2;
@@ -78,8 +82,37 @@ WsLayout make_layout(const Shape& s, int dtype) {
   w.ctrl = off;
   w.ctrl_bytes = tc_ctrl_bytes(s);
   off = align_up(off + w.ctrl_bytes, 256);
+  if (conv) {
+    const size_t rows = heads * (size_t)s.N;
+    w.xq = off; off = align_up(off + rows * s.D * 2, 256);
+    w.xk = off; off = align_up(off + rows * s.D * 2, 256);
+    w.xv = off; off = align_up(off + rows * s.Dv * 2, 256);
+  }
   w.total = off;
   return w;
+}
+
+// The bf16 problem an e4m3 call is run as on the tensor-core kernels: q, k, v
+// replaced by their dequantised contiguous copies in the workspace (null
+// pointers when `ws` is null, for shape-only checks).
+ma_fwd_params bf16_view(const ma_fwd_params* p, const Shape& s, char* ws, const WsLayout& w) {
+  ma_fwd_params v = *p;
+  v.dtype = MA_DTYPE_BF16;
+  v.out_dtype = MA_DTYPE_BF16;
+  v.q = ws ? ws + w.xq : nullptr;
+  v.k = ws ? ws + w.xk : nullptr;
+  v.v = ws ? ws + w.xv : nullptr;
+  if (!ws) v.out = nullptr;
+  const int64_t n = s.N;
+  const int64_t rq[4] = {(int64_t)s.H * n * s.D, n * s.D, s.D, 1};
+  const int64_t rv[4] = {(int64_t)s.H * n * s.Dv, n * s.Dv, s.Dv, 1};
+  for (int i = 0; i < 4; ++i) {
+    v.q_stride[i] = rq[i];
+    v.k_stride[i] = rq[i];
+    v.v_stride[i] = rv[i];
+  }
+  v.q_scale = v.k_scale = v.v_scale = nullptr;
+  return v;
 }
 
 // Host-side validation; nothing is launched when this fails.
@@ -119,7 +152,30 @@ int validate(const ma_fwd_params* p, bool need_buffers) {
 }
 
 // Picks the kernel family; returns MA_OK and sets *impl, or an error code.
+// e4m3 problems are checked as their bf16 view (`view`): the tensor-core
+// kernels run them after a conversion launch, the generic kernels directly.
 int select_impl(const ma_fwd_params* p, const Shape& s, int* impl) {
+  if (p->dtype == MA_DTYPE_E4M3 && p->impl != MA_IMPL_GENERIC) {
+    const ma_fwd_params v = bf16_view(p, s, nullptr, WsLayout{});
+    // the view has no buffers yet; the output pointer is the caller's
+    ma_fwd_params vo = v;
+    vo.out = p->out;
+    // (tc_supports checks the output alignment only together with q / k / v)
+    const bool out16 = p->out == nullptr || (reinterpret_cast<uintptr_t>(p->out) & 15) == 0;
+    const bool tc = tc_supports(&vo, s) && out16, sm = small_supports(&vo, s);
+    if (p->impl == MA_IMPL_TC && !tc)
+      return fail(MA_ERR_UNSUPPORTED, "the tcgen05 kernel does not support this shape");
+    if (p->impl == MA_IMPL_SMALL && !sm)
+      return fail(MA_ERR_UNSUPPORTED, "the small-block kernel does not support this shape");
+    if (p->impl == MA_IMPL_TC || (p->impl == MA_IMPL_AUTO && tc)) {
+      *impl = MA_IMPL_TC;
+      return MA_OK;
+    }
+    if (p->impl == MA_IMPL_SMALL || (p->impl == MA_IMPL_AUTO && sm)) {
+      *impl = MA_IMPL_SMALL;
+      return MA_OK;
+    }
+  }
   const bool tc = tc_supports(p, s);
   if (p->impl == MA_IMPL_TC) {
     if (!tc) return fail(MA_ERR_UNSUPPORTED, "the tcgen05 kernel does not support this shape");
@@ -156,9 +212,20 @@ void set_error_detail(const std::string& detail) { g_detail = detail; }
 
 extern "C" {
 
+// e4m3 calls that run on a tensor-core kernel need the bf16 copies
+bool needs_conversion(const ma_fwd_params* p, const Shape& s) {
+  if (p->dtype != MA_DTYPE_E4M3) return false;
+  int impl = 0;
+  const std::string keep = g_detail;
+  const bool ok = select_impl(p, s, &impl) == MA_OK;
+  g_detail = keep;
+  return ok && impl != MA_IMPL_GENERIC;
+}
+
 size_t ma_workspace_bytes(const ma_fwd_params* p) {
   if (validate(p, false) != MA_OK) return 0;
-  return make_layout(make_shape(p), p->dtype).total;
+  const Shape s = make_shape(p);
+  return make_layout(s, p->dtype, needs_conversion(p, s)).total;
 }
 
 int ma_select_impl(const ma_fwd_params* p) {
@@ -176,18 +243,29 @@ int ma_fwd(const ma_fwd_params* p, void* stream) {
   int rc = validate(p, true);
   if (rc != MA_OK) return rc;
   const Shape s = make_shape(p);
-  const WsLayout ws = make_layout(s, p->dtype);
-  if (p->workspace == nullptr || p->workspace_bytes < ws.total)
-    return fail(MA_ERR_WORKSPACE, "workspace needs " + std::to_string(ws.total) + " bytes, got " +
-                                      std::to_string(p->workspace_bytes));
   int impl = 0;
   rc = select_impl(p, s, &impl);
   if (rc != MA_OK) return rc;
+  const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
+  const WsLayout ws = make_layout(s, p->dtype, conv);
+  if (p->workspace == nullptr || p->workspace_bytes < ws.total)
+    return fail(MA_ERR_WORKSPACE, "workspace needs " + std::to_string(ws.total) + " bytes, got " +
+                                      std::to_string(p->workspace_bytes));
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int n = 0;
-  cudaError_t err = impl == MA_IMPL_TC      ? run_tc(p, s, ws, st, &n)
-                    : impl == MA_IMPL_SMALL ? run_small(p, s, ws, st, &n)
-                                            : run_generic(p, s, ws, st, &n);
+  cudaError_t err = cudaSuccess;
+  ma_fwd_params view;
+  const ma_fwd_params* run = p;
+  if (conv) {  // dequantise into the bf16 copies, then run the bf16 problem
+    char* w = reinterpret_cast<char*>(p->workspace);
+    view = bf16_view(p, s, w, ws);
+    run = &view;
+    err = run_e4m3_to_bf16(p, s, w + ws.xq, w + ws.xk, w + ws.xv, st, &n);
+  }
+  if (err == cudaSuccess)
+    err = impl == MA_IMPL_TC      ? run_tc(run, s, ws, st, &n)
+          : impl == MA_IMPL_SMALL ? run_small(run, s, ws, st, &n)
+                                  : run_generic(run, s, ws, st, &n);
   if (err != cudaSuccess)
     return fail(MA_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorName(err) + ": " +
                                  cudaGetErrorString(err));

@@ -34,8 +34,11 @@ struct Shape {
 //   cl [b][M] fp32, cr [M][b] fp32  -- row/column statistics
 //   lmax, lsum [b][M] fp32          -- L-step softmax statistics (generic path)
 //   ctrl                            -- dependency counters (tcgen05 path)
+//   xq, xk, xv                      -- bf16 copies of e4m3 q / k / v for the
+//                                      tensor-core kernels (0 = not used)
 struct WsLayout {
   size_t al, y, ar, cl, cr, lmax, lsum, ctrl, ctrl_bytes, total;
+  size_t xq, xk, xv;
   int store_bytes;  // bytes per element of al / y / ar
 };
 

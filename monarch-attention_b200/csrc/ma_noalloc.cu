@@ -108,7 +108,9 @@ ma::WsLayout compact_layout(const ma::Shape& s, int slots, size_t* status_off) {
 extern "C" int ma_fwd_noalloc(const ma_fwd_params* p, void* stream) {
   const int sel = ma_select_impl(p);  // validates the parameter block
   if (sel < 0) return -sel;
-  if (sel != MA_IMPL_TC) {
+  // e4m3 inputs reach the tcgen05 kernel only through bf16 copies in a
+  // caller workspace, which this entry point does not have
+  if (sel != MA_IMPL_TC || (p->dtype != MA_DTYPE_BF16 && p->dtype != MA_DTYPE_F16)) {
     ma::set_error_detail(
         "ma_fwd_noalloc runs the tcgen05 kernel only (block size = blocks = head dim = 128, "
         "bf16/fp16, no mask); use ma_fwd for this shape");

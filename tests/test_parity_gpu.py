@@ -216,12 +216,20 @@ def test_missing_library_fails_loudly(monkeypatch, cuda_device):
 # float8 e4m3 inputs with per-(e, h) scales: compared with the fp32 oracle run
 # on the dequantised inputs (the quantisation error itself is not counted)
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("name,shape", [("long4k_e4m3", dict(E=1, H=2)),
-                                        ("long16k_e4m3", dict(E=1, H=1))])
-def test_e4m3_against_dequantised_oracle(name, shape, cuda_device):
+E4M3_CASES = [("long4k_e4m3", dict(E=1, H=2), "auto"),
+              ("long16k_e4m3", dict(E=1, H=1), "auto"),
+              ("long16k_e4m3", dict(E=1, H=1), "generic"),
+              ("long16k_e4m3", dict(E=1, H=3), "tc"),
+              ("vit_bf16", dict(E=2, H=2, dtype="e4m3"), "small"),
+              ("roberta_bf16", dict(E=2, H=2, dtype="e4m3"), "small")]
+
+
+@pytest.mark.parametrize("name,shape,impl", E4M3_CASES,
+                         ids=[f"{n}-{i}-{sh.get('H')}" for n, sh, i in E4M3_CASES])
+def test_e4m3_against_dequantised_oracle(name, shape, impl, cuda_device):
     cfg = CONFIGS[name].with_(**shape)
     q, k, v, mask, scales = make_inputs(cfg, device=cuda_device)
-    out = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, scales=scales)
+    out = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, scales=scales, impl=impl)
     torch.cuda.synchronize()
     check_status(cuda_device)
     assert out.dtype == torch.bfloat16
@@ -231,3 +239,30 @@ def test_e4m3_against_dequantised_oracle(name, shape, cuda_device):
     err = np.abs(got - ref).max()
     assert np.isfinite(got).all()
     assert err <= E4M3_TOL * float(np.abs(ref).max()), f"max|err|={err:.3g}"
+
+
+def test_e4m3_routes_to_tensor_core_kernels(cuda_device):
+    """e4m3 inputs run on the tensor-core kernels after a bf16 conversion."""
+    for name, shape, want in [("long16k_e4m3", dict(E=1, H=1), "tc"),
+                              ("vit_bf16", dict(E=1, H=1, dtype="e4m3"), "small"),
+                              ("long4k_e4m3", dict(E=1, H=1), "generic")]:
+        cfg = CONFIGS[name].with_(**shape)
+        q, k, v, mask, _ = make_inputs(cfg, device=cuda_device)
+        assert mab.selected_impl(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad) == want, name
+
+
+def test_e4m3_full_size_tc(cuda_device):
+    """long16k e4m3 at full size through the conversion + tcgen05 route."""
+    cfg = CONFIGS["long16k_e4m3"]
+    q, k, v, mask, scales = make_inputs(cfg, device=cuda_device)
+    out = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, scales=scales)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert torch.isfinite(out.float()).all()
+    for e, h in ((0, 0), (cfg.E - 1, cfg.H - 1)):
+        sl = (slice(e, e + 1), slice(h, h + 1))
+        deq = [dequantize_e4m3(t[sl], s_[sl]) for t, s_ in zip((q, k, v), scales)]
+        ref = oracle_for(*deq, None, cfg, "f32")
+        got = out[sl].float().cpu().numpy()
+        err = np.abs(got - ref).max()
+        assert err <= E4M3_TOL * float(np.abs(ref).max()), f"head ({e},{h}): max|err|={err:.3g}"
