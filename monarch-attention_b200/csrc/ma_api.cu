@@ -81,6 +81,7 @@ WsLayout make_layout(const Shape& s, int dtype, bool conv) {
   w.lsum = off; off = align_up(off + heads * bm * 4, 256);
   w.ctrl = off;
   w.ctrl_bytes = tc_ctrl_bytes(s);
+  w.tc_slots = (int)heads;
   off = align_up(off + w.ctrl_bytes, 256);
   if (conv) {
     const size_t rows = heads * (size_t)s.N;

@@ -36,9 +36,14 @@ struct Shape {
 //   ctrl                            -- dependency counters (tcgen05 path)
 //   xq, xk, xv                      -- bf16 copies of e4m3 q / k / v for the
 //                                      tensor-core kernels (0 = not used)
+//   tc_slots                         -- heads whose al / y / ar / cl / cr
+//                                      arrays exist (the tcgen05 kernel's
+//                                      slot limit; every head in ma_fwd's
+//                                      workspace, fewer in compact ones)
 struct WsLayout {
   size_t al, y, ar, cl, cr, lmax, lsum, ctrl, ctrl_bytes, total;
   size_t xq, xk, xv;
+  int tc_slots;
   int store_bytes;  // bytes per element of al / y / ar
 };
 

@@ -1255,8 +1255,14 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   if (hg) hgroup = atoi(hg);
   if (hgroup < 1) hgroup = 1;
   if (hgroup > nheads) hgroup = nheads;
+  // The workspace holds the arrays of ws.tc_slots heads.  A slot is reused
+  // by head h + slots once head h's output phase is done, so a group of
+  // hgroup heads needs hgroup * (2T + 1) slots to keep dependencies pointing
+  // to earlier rounds of the wavefront: shrink the group to what exists.
+  const int max_slots = ws.tc_slots > 0 && ws.tc_slots < nheads ? ws.tc_slots : nheads;
+  if (hgroup * (2 * s.T + 1) > max_slots) hgroup = max_slots / (2 * s.T + 1) > 1 ? max_slots / (2 * s.T + 1) : 1;
   int slots = hgroup * (2 * s.T + 1);
-  if (slots > nheads) slots = nheads;
+  if (slots > max_slots) slots = max_slots;
   const uint32_t box_blk[4] = {64, kT, 1, 1};
   const uint32_t box_str[5] = {64, 1, kT, 1, 1};
   const uint32_t box_ws[2] = {64, kT};

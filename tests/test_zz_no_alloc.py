@@ -33,9 +33,12 @@ def noalloc_fn():
 
 
 @pytest.mark.gpu
-def test_noalloc_matches_ma_fwd_twice(cuda_device):
+@pytest.mark.parametrize("H", [3, 8])
+def test_noalloc_matches_ma_fwd_twice(H, cuda_device):
+    """H = 8 heads is more than the 2T + 1 = 5 slots the scratch holds: the
+    kernel must then cycle through those 5 slots only."""
     lib, fn = noalloc_fn()
-    cfg = CONFIGS["long16k_bf16"].with_(E=1, H=3)
+    cfg = CONFIGS["long16k_bf16"].with_(E=1, H=H)
     stream = torch.cuda.current_stream(cuda_device)
     for call, seed in enumerate((11, 12)):
         q, k, v, mask, _ = make_inputs(cfg, device=cuda_device, seed=seed)
