@@ -591,8 +591,17 @@ __device__ __forceinline__ void gemm2_ts(uint32_t tO, uint32_t tP, uint32_t X) {
     mma_ts(tO, tP + kk * 8, smem_desc(X + kk * 2048, kHalf, 1024, kSwz128), id_ts, kk > 0);
 }
 
-template <bool BF16>
+// BLK: block size b = number of blocks M (128 or 64).  A work item is one
+// 128-row tile holding PACK = 128 / BLK items of the reference (key blocks m
+// of an R-step, indices j of an L / output step) stacked on top of each
+// other; for BLK = 64 both GEMMs run block-diagonally over the full tile
+// (the off-diagonal products are not used: the softmax covers each row's
+// own 64-column block and sets P to zero elsewhere).
+template <bool BF16, int BLK>
 __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constant__ TcParams p) {
+  constexpr int PACK = kT / BLK;          // items per tile
+  constexpr int kTiles = BLK * BLK / kT;  // tiles per (head, phase)
+  static_assert(PACK == 1 || PACK == 2, "block size 64 or 128");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t sbase = smem_u32(smem_raw);                       // small objects
   const uint32_t tbase = (sbase + kSmallBytes + 1023u) & ~1023u;   // SW128 tiles
@@ -601,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
   uint32_t* ctrl = p.ctrl;
   const Guard guard{ctrl + kCtrlAbort, p.status, p.timeout_ns};
   const int P = p.P;
-  const uint32_t total = (uint32_t)p.nheads * P * kT;
+  const uint32_t total = (uint32_t)p.nheads * P * kTiles;
 
   int4* desc_slot = reinterpret_cast<int4*>(smem_raw + kOffDesc);
   int4* item_ring = reinterpret_cast<int4*>(smem_raw + kOffItems);
@@ -670,8 +679,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         bool ok = w < total && !ld_relaxed(guard.abort);
         int head = -1, item = 0, kind = 0;
         if (ok) {
-          const uint32_t want = w / kT;
-          item = (int)(w % kT);
+          const uint32_t want = w / kTiles;
+          item = (int)(w % kTiles);
           while (blk < want) {
             ++sub;
             if (sub >= G || G * (r - ph) + sub >= p.nheads) {
@@ -695,9 +704,9 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           // dependency: the previous phase of this head, or -- for phase 0 --
           // the output phase of the head that used this workspace slot before
           if (ph > 0)
-            ok = wait_counter(ctrl + kCtrlDone + head * P + ph - 1, (uint32_t)kT, guard);
+            ok = wait_counter(ctrl + kCtrlDone + head * P + ph - 1, (uint32_t)kTiles, guard);
           else if (head >= p.slots)
-            ok = wait_counter(ctrl + kCtrlDone + (head - p.slots) * P + P - 1, (uint32_t)kT,
+            ok = wait_counter(ctrl + kCtrlDone + (head - p.slots) * P + P - 1, (uint32_t)kTiles,
                               guard);
         }
         if (p.early && n >= kEntries && !wait_bar(bar(kBarEmpty, e), (use - 1) & 1, guard))
@@ -716,7 +725,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const int eb = head / p.H, hh = head - eb * p.H;
         const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
         const uint32_t vdst = sbase + kOffVec + e * 512;
-        const size_t vrow = ((size_t)slot * kT + item) * kT;  // cr[slot][m][:] / cl[slot][j][:]
+        // first row of the tile in the per-slot arrays ar [M][b], al / y
+        // [b][M], cr [M][b], cl [b][M] (rows of D / Dv elements or floats),
+        // and its first token in q / k / v
+        const int trow = slot * BLK * BLK + item * kT;
+        const int tok0 = item * kT;
+        const size_t vrow = (size_t)trow;
         // L2 policy: keep what a later phase of this head reads again (q before
         // the output phase, k before the final R-step); stream last uses and
         // the single-use intermediates
@@ -728,10 +742,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             if (first)
-              tma_load_4d_h(A + h2 * kHalf, &p.tm_qblk, h2 * 64, item * kT, hh, eb, fb, keep);
+              tma_load_4d_h(A + h2 * kHalf, &p.tm_qblk, h2 * 64, tok0, hh, eb, fb, keep);
             else
-              tma_load_2d_h(A + h2 * kHalf, &p.tm_ar, h2 * 64, (slot * kT + item) * kT, fb, once);
-            tma_load_4d_h(B + h2 * kHalf, &p.tm_kblk, h2 * 64, item * kT, hh, eb, fb,
+              tma_load_2d_h(A + h2 * kHalf, &p.tm_ar, h2 * 64, trow, fb, once);
+            tma_load_4d_h(B + h2 * kHalf, &p.tm_kblk, h2 * 64, tok0, hh, eb, fb,
                           final_ ? once : keep);
           }
         } else {
@@ -739,9 +753,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           bulk_load(vdst, p.cl + vrow, 512, fb);
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
-            tma_load_5d_h(A + h2 * kHalf, &p.tm_qstr, h2 * 64, item, 0, hh, eb, fb,
-                          kind == KIND_O ? once : keep);
-            tma_load_2d_h(B + h2 * kHalf, &p.tm_al, h2 * 64, (slot * kT + item) * kT, fb, once);
+            // Q_j: tokens j, j + b, j + 2b, ... of each index j of the tile
+#pragma unroll
+            for (int pk = 0; pk < PACK; ++pk)
+              tma_load_5d_h(A + h2 * kHalf + pk * BLK * 128, &p.tm_qstr, h2 * 64,
+                            item * PACK + pk, 0, hh, eb, fb, kind == KIND_O ? once : keep);
+            tma_load_2d_h(B + h2 * kHalf, &p.tm_al, h2 * 64, trow, fb, once);
           }
         }
         issued |= 1u << e;
@@ -909,6 +926,11 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       const int eb = head / p.H, hh = head - eb * p.H;
       const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
       const float* vec = vec0 + e * 128;  // cr[m][:] (R) or cl[j][:] (L / out)
+      const int trow = slot * BLK * BLK + item * kT;  // tile's first row in the slot arrays
+      // the item of this row within the tile and, for BLK = 64, the 64-column
+      // half of S / P that belongs to it (warp-uniform: 64 rows = 2 warps)
+      const int pk_row = row / BLK;
+      const int h_lo = PACK == 1 ? 0 : pk_row, h_hi = PACK == 1 ? 2 : pk_row + 1;
 
       // late X tile (V[m] for R-final, y_j for out) into tile A, free after GEMM1
       if ((final_ || kind == KIND_O) && row == 0) {
@@ -921,19 +943,18 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           if (final_)
             tma_load_4d_h(A + h2 * kHalf, &p.tm_vblk, h2 * 64, item * kT, hh, eb, xb, once);
           else
-            tma_load_2d_h(A + h2 * kHalf, &p.tm_y, h2 * 64, (slot * kT + item) * kT, xb, once);
+            tma_load_2d_h(A + h2 * kHalf, &p.tm_y, h2 * 64, trow, xb, once);
         }
       }
 
       // The intermediate tiles and vectors this item read have no other
       // reader: drop them from L2 so their dirty lines are never written back
       if (kind != KIND_R || ph > 0) {
-        const char* tile = (kind == KIND_R ? p.ar : p.al) + ((size_t)slot * kT + item) * kT * kT * 2;
+        const char* tile = (kind == KIND_R ? p.ar : p.al) + (size_t)trow * kT * 2;
         discard_l2(tile + row * 128);
         discard_l2(tile + (row + 128) * 128);
         if (row < 4)
-          discard_l2(reinterpret_cast<const char*>((kind == KIND_R ? p.cr : p.cl) +
-                                                   ((size_t)slot * kT + item) * kT) + row * 128);
+          discard_l2(reinterpret_cast<const char*>((kind == KIND_R ? p.cr : p.cl) + trow) + row * 128);
       }
 
       // The row of S (128 fp32) is streamed out of TMEM in 64-column halves:
@@ -947,7 +968,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       {
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
-        for (int h2 = 0; h2 < 2; ++h2) {
+        for (int h2 = h_lo; h2 < h_hi; ++h2) {
           uint32_t sv[64];
           tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
           tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
@@ -977,7 +998,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       }
       float s4[4] = {0.f, 0.f, 0.f, 0.f}, w4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-      for (int h2 = 0; h2 < 2; ++h2) {
+      for (int h2 = h_lo; h2 < h_hi; ++h2) {
         uint32_t sv[64];
         tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
         tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
@@ -1005,6 +1026,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           tmem_st32(tS + 32 * h2, pk);
         }
       }
+      if (PACK == 2 && kind != KIND_L) {  // P of the other item's block is zero
+        uint32_t z[32];
+#pragma unroll
+        for (int c2 = 0; c2 < 32; ++c2) z[c2] = 0u;
+        tmem_st32(tS + 32 * (1 - pk_row), z);
+      }
       tmem_wait_st();
       const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       float scale_out;
@@ -1013,7 +1040,9 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const float den = sum + kEps;  // r = e / (sum + eps), :17
         const float inv = 1.0f / den;
         // cl = sum_i r_i log r_i, log r_i = (t_i - mx) - log(den)  (:20)
-        p.cl[((size_t)slot * kT + row) * kT + item] = kLn2 * inv * wsum - __logf(den) * sum * inv;
+        // cl[j][m] of this row: j = row % BLK, m = the row's key block
+        p.cl[(size_t)(slot * BLK + row % BLK) * BLK + item * PACK + pk_row] =
+            kLn2 * inv * wsum - __logf(den) * sum * inv;
         scale_out = inv;
       } else {
         scale_out = 1.0f / sum;
@@ -1025,8 +1054,13 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         // consumed) in the MN-major SW128 layout: row l of half h at
         // h*16K + l*128, 16-byte chunk c at position c ^ (l & 7)
         const uint32_t prow = B + row * 128;
+        if (PACK == 2) {  // the other item's columns of the row are zero
+#pragma unroll
+          for (int cc = 0; cc < 8; ++cc)
+            st_shared_v4(prow + (1 - pk_row) * kHalf + ((cc ^ (row & 7)) << 4), 0u, 0u, 0u, 0u);
+        }
 #pragma unroll 1
-        for (int h2 = 0; h2 < 2; ++h2) {
+        for (int h2 = h_lo; h2 < h_hi; ++h2) {
           uint32_t sv[64];
           tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
           tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
@@ -1090,14 +1124,15 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(bar(kBarCrTaken, g));
-        p.cr[((size_t)slot * kT + row) * kT + item] = __uint_as_float(o[0]);
+        // cr[k][j] of this row: k = row % BLK, j = the row's index
+        p.cr[(size_t)(slot * BLK + row % BLK) * BLK + item * PACK + row / BLK] = __uint_as_float(o[0]);
         // ar[k][j] = sum_l P[l][k] q[l*b+j] (:34)
         stage_row128<BF16>(A, row, tO, 1.0f);
       } else {
         // z[l*b + j] = (P y_j) / sum (ma_torch.py:60-62)
         stage_row128<BF16>(A, row, tO, scale_out);
         // y_j has no other reader: drop it from L2 (GEMM2 consumed it)
-        const char* ytile = p.y + ((size_t)slot * kT + item) * kT * kT * 2;
+        const char* ytile = p.y + ((size_t)slot * BLK * BLK + item * kT) * kT * 2;
         discard_l2(ytile + row * 128);
         discard_l2(ytile + (row + 128) * 128);
       }
@@ -1145,17 +1180,22 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         // intermediates are read by the next phase soon: keep them in L2;
         // the output streams out
         const uint64_t keep = policy_evict_last(), once = policy_evict_first();
+        // one box of BLK rows per item of the tile: al[.][m] (rows j), y[.][m],
+        // ar[.][j] (rows k), out tokens l*b + j
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          if (kind == KIND_R) {
-            tma_store_3d_h(&p.tm_al_st, (final_ ? B : A) + h2 * kHalf, h2 * 64, item, slot * kT,
-                           keep);
-            if (final_)
-              tma_store_3d_h(&p.tm_y_st, A + h2 * kHalf, h2 * 64, item, slot * kT, keep);
-          } else if (kind == KIND_L) {
-            tma_store_3d_h(&p.tm_ar_st, A + h2 * kHalf, h2 * 64, item, slot * kT, keep);
-          } else {
-            tma_store_5d_h(&p.tm_out_st, A + h2 * kHalf, h2 * 64, item, 0, hh, eb, once);
+#pragma unroll
+          for (int pk = 0; pk < PACK; ++pk) {
+            const int it = item * PACK + pk;
+            const uint32_t off = h2 * kHalf + pk * BLK * 128;
+            if (kind == KIND_R) {
+              tma_store_3d_h(&p.tm_al_st, (final_ ? B : A) + off, h2 * 64, it, slot * BLK, keep);
+              if (final_) tma_store_3d_h(&p.tm_y_st, A + off, h2 * 64, it, slot * BLK, keep);
+            } else if (kind == KIND_L) {
+              tma_store_3d_h(&p.tm_ar_st, A + off, h2 * 64, it, slot * BLK, keep);
+            } else {
+              tma_store_5d_h(&p.tm_out_st, A + off, h2 * 64, it, 0, hh, eb, once);
+            }
           }
         }
         bulk_commit();
@@ -1222,7 +1262,8 @@ bool tc_supports(const ma_fwd_params* p, const Shape& s) {
   const char* off = getenv("MA_DISABLE_TC");
   if (off && off[0] == '1') return false;
   if (p->dtype != MA_DTYPE_BF16 && p->dtype != MA_DTYPE_F16) return false;
-  if (s.D != 128 || s.Dv != 128 || s.b != 128 || s.M != 128 || s.N != s.Np) return false;
+  if (s.D != 128 || s.Dv != 128 || s.N != s.Np) return false;
+  if (!((s.b == 128 && s.M == 128) || (s.b == 64 && s.M == 64))) return false;
   if (p->mask_dtype != MA_MASK_NONE) return false;
   const int64_t* st[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
   for (int t = 0; t < 4; ++t) {
@@ -1250,7 +1291,11 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   const int P = 2 * s.T;
   // heads per wavefront phase slot: more heads in flight -> a longer distance
   // between dependent items (a round is 2T * hgroup * 128 items)
-  int hgroup = 2;  // measured best on B200 (1: 856 us, 2: 785 us, 3: 808 us, 4: 803 us)
+  // tiles per (head, phase): 128 for b = 128, 32 for b = 64 (two items per tile)
+  const int tiles = s.b * s.b / tc::kT;
+  // measured best on B200 for b = 128 (1: 856 us, 2: 785 us, 3: 808 us,
+  // 4: 803 us); the same round length (1024 tiles) for b = 64
+  int hgroup = 256 / tiles;
   const char* hg = getenv("MA_TC_GROUP");
   if (hg) hgroup = atoi(hg);
   if (hgroup < 1) hgroup = 1;
@@ -1264,7 +1309,7 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   int slots = hgroup * (2 * s.T + 1);
   if (slots > max_slots) slots = max_slots;
   const uint32_t box_blk[4] = {64, kT, 1, 1};
-  const uint32_t box_str[5] = {64, 1, kT, 1, 1};
+  const uint32_t box_str[5] = {64, 1, (uint32_t)s.M, 1, 1};
   const uint32_t box_ws[2] = {64, kT};
   bool ok = true;
   auto tok_map = [&](CUtensorMap* tm, const void* base, const int64_t* es) {
@@ -1296,7 +1341,7 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   }
   {
     // store views: 64 x 1 x 128 boxes of strided rows
-    const uint32_t box3[3] = {64, 1, kT};
+    const uint32_t box3[3] = {64, 1, (uint32_t)s.b};
     const uint64_t dal[3] = {(uint64_t)s.D, (uint64_t)s.M, (uint64_t)slots * s.b};
     const uint64_t sal[2] = {(uint64_t)s.D * 2, (uint64_t)s.M * s.D * 2};
     ok = ok && encode(&tp.tm_al_st, dt, 3, w + ws.al, dal, sal, box3);
@@ -1311,7 +1356,7 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
                               (uint64_t)s.E};
     const uint64_t sout[4] = {(uint64_t)os[2] * 2, (uint64_t)os[2] * 2 * s.b,
                               (uint64_t)os[1] * 2, (uint64_t)os[0] * 2};
-    const uint32_t box5[5] = {64, 1, kT, 1, 1};
+    const uint32_t box5[5] = {64, 1, (uint32_t)s.M, 1, 1};
     ok = ok && encode(&tp.tm_out_st, dt, 5, p->out, dout, sout, box5);
   }
   if (!ok) return cudaErrorInvalidValue;
@@ -1348,10 +1393,12 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   if (err != cudaSuccess) return err;
   err = cudaMemsetAsync(tp.ctrl, 0, ws.ctrl_bytes, st);
   if (err != cudaSuccess) return err;
-  auto kfn = p->dtype == MA_DTYPE_BF16 ? ma_tc_kernel<true> : ma_tc_kernel<false>;
+  const bool bf = p->dtype == MA_DTYPE_BF16;
+  auto kfn = s.b == 128 ? (bf ? ma_tc_kernel<true, 128> : ma_tc_kernel<false, 128>)
+                        : (bf ? ma_tc_kernel<true, 64> : ma_tc_kernel<false, 64>);
   err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (err != cudaSuccess) return err;
-  const int64_t items = (int64_t)nheads * P * kT;
+  const int64_t items = (int64_t)nheads * P * tiles;
   const int grid = (int)(items < sms ? items : sms);
   kfn<<<grid, kThreads, kSmemBytes, st>>>(tp);
   err = cudaGetLastError();

@@ -244,8 +244,9 @@ def test_e4m3_against_dequantised_oracle(name, shape, impl, cuda_device):
 def test_e4m3_routes_to_tensor_core_kernels(cuda_device):
     """e4m3 inputs run on the tensor-core kernels after a bf16 conversion."""
     for name, shape, want in [("long16k_e4m3", dict(E=1, H=1), "tc"),
+                              ("long4k_bf16", dict(E=1, H=1), "tc"),
                               ("vit_bf16", dict(E=1, H=1, dtype="e4m3"), "small"),
-                              ("long4k_e4m3", dict(E=1, H=1), "generic")]:
+                              ("long4k_e4m3", dict(E=1, H=1), "tc")]:
         cfg = CONFIGS[name].with_(**shape)
         q, k, v, mask, _ = make_inputs(cfg, device=cuda_device)
         assert mab.selected_impl(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad) == want, name
