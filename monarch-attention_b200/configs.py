@@ -52,6 +52,9 @@ CONFIGS = {
     for c in [
         Config("cfg0_f32", 2, 12, 256, 64, 16, 3, "f32", seed=1000),
         Config("vit_bf16", 64, 12, 196, 64, 14, 2, "bf16", seed=1001),
+        # the ViT pipeline itself: 197 tokens (CLS + 14 x 14 patches), fp16,
+        # padded at the front to 15 blocks of 14 (vit/benchmark.py:19-25)
+        Config("vit_n197_f16", 64, 12, 197, 64, 14, 2, "f16", pre_pad=True, seed=1005),
         Config("roberta_bf16", 32, 12, 512, 64, 32, 2, "bf16", mask_min_len=128, seed=1002),
         Config("dit_bf16", 32, 16, 1024, 72, 32, 3, "bf16", seed=1003),
         Config("long4k_bf16", 4, 16, 4096, 128, 64, 2, "bf16", scaled=False, seed=1004),

@@ -179,6 +179,12 @@ def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None,
     pre_pad selecting front padding.  Returns a new contiguous (E, H, N, Dv)
     tensor in v.dtype (bf16 for float8_e4m3fn inputs, which also need
     ``scales=(q_scale, k_scale, v_scale)``, each (E, H) fp32).
+
+    ``out`` (optional) receives the result instead of a new tensor: an
+    (E, H, N, Dv) tensor of the output dtype with any strides, e.g. the
+    ``(E, N, H, Dv)`` buffer of the next projection seen through
+    ``.permute(0, 2, 1, 3)``; with q, k, v passed as the same kind of views
+    of the (E, N, H*D) projections, no layout copy is made on either side.
     """
     _check_inputs(q, k, v)
     E, H, N, _ = q.shape
@@ -188,6 +194,13 @@ def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None,
         raise ValueError("float8_e4m3fn inputs need scales=(q_scale, k_scale, v_scale)")
     if out is None:
         out = torch.empty((E, H, N, Dv), dtype=out_dtype, device=q.device)
+    else:
+        if tuple(out.shape) != (E, H, N, Dv):
+            raise ValueError(f"out shape {tuple(out.shape)} != {(E, H, N, Dv)}")
+        if out.dtype != out_dtype:
+            raise TypeError(f"out dtype {out.dtype} != {out_dtype}")
+        if out.device != q.device:
+            raise ValueError("out is on a different device than the inputs")
     lib = _lib.load()
     p, keep = build_params(q, k, v, out, attn_mask, T, B, pre_pad, _impl_code(impl), scales)
     nbytes = lib.ma_workspace_bytes(ctypes.byref(p))

@@ -72,6 +72,7 @@ def test_golden(path, impl, cuda_device):
 SMALL = {
     "cfg0_f32": dict(),
     "vit_bf16": dict(E=2, H=2),
+    "vit_n197_f16": dict(E=2, H=2),
     "roberta_bf16": dict(E=3, H=2),
     "dit_bf16": dict(E=1, H=2),
     "long4k_bf16": dict(E=1, H=2),
@@ -106,7 +107,8 @@ def test_config_small(name, impl, cuda_device):
 # ---------------------------------------------------------------------------
 # full-size configs: every head computed, a sample of heads checked exactly
 # ---------------------------------------------------------------------------
-FULL = ["cfg0_f32", "vit_bf16", "roberta_bf16", "dit_bf16", "long4k_bf16", "long16k_bf16"]
+FULL = ["cfg0_f32", "vit_bf16", "vit_n197_f16", "roberta_bf16", "dit_bf16", "long4k_bf16",
+        "long16k_bf16"]
 
 
 @pytest.mark.parametrize("name", FULL)
@@ -140,6 +142,42 @@ def test_permuted_views_match_contiguous(cuda_device):
     b = monarch_attention(*[t.contiguous() for t in views], None, 2, 16, False)
     assert torch.equal(a, b)
     assert a.is_contiguous()
+
+
+@pytest.mark.parametrize("impl,shape", [("small", (2, 3, 196, 64, 14)),
+                                        ("generic", (2, 3, 196, 64, 14)),
+                                        ("tc", (1, 2, 16384, 128, 128)),
+                                        ("tc", (1, 2, 4096, 128, 64))])
+def test_caller_layout_in_and_out(impl, shape, cuda_device):
+    """Projections in the callers' (E, N, H*D) layout are read through
+    permuted views and the result is written straight into an (E, N, H*Dv)
+    buffer (vit/model.py:93-101): no layout copy on either side."""
+    E, H, N, D, b = shape
+    g = torch.Generator(device="cpu").manual_seed(21)
+    proj = [torch.randn(E, N, H * D, generator=g).to(cuda_device, torch.bfloat16)
+            for _ in range(3)]
+    if D == 64:
+        proj = [t / 8 for t in proj]
+    q, k, v = (t.view(E, N, H, D).permute(0, 2, 1, 3) for t in proj)
+    o_buf = torch.full((E, N, H * D), float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    o_view = o_buf.view(E, N, H, D).permute(0, 2, 1, 3)
+    assert mab.selected_impl(q, k, v, None, 2, b, False, impl=impl) == impl
+    res = monarch_attention(q, k, v, None, 2, b, False, impl=impl, out=o_view)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert res.data_ptr() == o_buf.data_ptr()
+    ref = monarch_attention(q.contiguous(), k.contiguous(), v.contiguous(), None, 2, b, False,
+                            impl=impl)
+    assert torch.equal(o_buf.view(E, N, H, D).permute(0, 2, 1, 3), ref)
+
+
+def test_out_argument_is_checked(cuda_device):
+    q = torch.randn(1, 2, 32, 16, device=cuda_device)
+    with pytest.raises(ValueError, match="out shape"):
+        monarch_attention(q, q, q, None, 2, 8, False, out=torch.empty(1, 2, 32, 8, device=cuda_device))
+    with pytest.raises(TypeError, match="out dtype"):
+        monarch_attention(q, q, q, None, 2, 8, False,
+                          out=torch.empty(1, 2, 32, 16, dtype=torch.float16, device=cuda_device))
 
 
 def test_mask_dtypes_agree(cuda_device):
