@@ -1,7 +1,9 @@
-// Fused small-block MonarchAttention forward: one CTA runs every phase of one
-// (batch, head) -- the T-1 (R, L) rounds, the final R-step and the output
-// step of ma/ma_torch.py:100-105 -- with __syncthreads between phases and
-// no kernel boundaries.  For block size b <= 32 and number of blocks M <= 32
+// Fused small-block MonarchAttention forward: one thread-block cluster runs
+// every phase of one (batch, head) -- the T-1 (R, L) rounds, the final
+// R-step and the output step of ma/ma_torch.py:100-105 -- with a cluster
+// barrier between phases and no kernel boundaries.  The cluster's CTAs (1, 2
+// or 4) take turns on the items of a phase, so a head's critical path is
+// shorter and the grid packs into fewer partial waves.  For block size b <= 32 and number of blocks M <= 32
 // (the ViT, RoBERTa and DiT shapes), D = Dv <= 128, bf16 / fp16, any strides,
 // padding and key-padding mask.
 //
@@ -15,6 +17,7 @@
 // (L-step, which contracts over rows).  Intermediates go through a per-head
 // workspace that stays in L2.
 #include <float.h>
+#include <stdlib.h>
 
 #include "ma_common.cuh"
 
@@ -448,13 +451,24 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
   __syncwarp();
 }
 
+// all threads of the cluster; orders the phase's global writes (release)
+// before the next phase's reads (acquire) across the cluster's CTAs
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+
 template <bool BF16, typename TI, int DP, int ROWS>
 __global__ void __launch_bounds__(kThreads, ROWS == 16 ? 4 : 3) ma_small_kernel(const SmallParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   using WT = WarpTiles<TI, DP, ROWS>;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int eh = blockIdx.x;
+  uint32_t crank, csize;  // this CTA's rank in its cluster, cluster size
+  asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  asm("mov.u32 %0, %%cluster_nctarank;" : "=r"(csize));
+  const int eh = blockIdx.x / csize;  // clusters are consecutive blocks
   const int e = eh / p.H, h = eh - e * p.H;
+  const int wg = crank * kWarps + warp, nw = csize * kWarps;  // warp within the cluster
   uint8_t* wsm = smem + warp * WT::kBytes;
   uint32_t* vbits = reinterpret_cast<uint32_t*>(smem + kWarps * WT::kBytes);
   // zero the tiles once: padding rows/columns must read as 0
@@ -473,21 +487,46 @@ __global__ void __launch_bounds__(kThreads, ROWS == 16 ? 4 : 3) ma_small_kernel(
   __syncthreads();
   for (int t = 0; t < p.T; ++t) {
     const bool final_ = t == p.T - 1;
-    for (int m = warp; m < p.M; m += kWarps) {
+    for (int m = wg; m < p.M; m += nw) {
       if (final_)
         run_item<PH_RF, BF16, TI, DP, ROWS>(p, e, h, m, t == 0, wsm, vbits, lane);
       else
         run_item<PH_R, BF16, TI, DP, ROWS>(p, e, h, m, t == 0, wsm, vbits, lane);
     }
-    __syncthreads();
-    for (int j = warp; j < p.b; j += kWarps) {
+    cluster_sync();
+    for (int j = wg; j < p.b; j += nw) {
       if (final_)
         run_item<PH_O, BF16, TI, DP, ROWS>(p, e, h, j, 0, wsm, vbits, lane);
       else
         run_item<PH_L, BF16, TI, DP, ROWS>(p, e, h, j, 0, wsm, vbits, lane);
     }
-    __syncthreads();
+    cluster_sync();
   }
+}
+
+// CTAs per head (1, 2 or 4).  CTAs of equal length run in waves of `slots`
+// (resident CTAs on the GPU), so a forward takes about
+// ceil(heads * C / slots) waves of 1 / C of a head's work; each doubling of
+// C costs ~10 % in cluster barriers and idle warps (a phase has only 14-32
+// items).  Measured on B200: ViT (768 heads) best at 2, RoBERTa (384 heads,
+// one wave) at 1, DiT (512 heads) at 4.  MA_SMALL_CLUSTER overrides.
+static int cluster_size(int heads, int slots) {
+  const char* env = getenv("MA_SMALL_CLUSTER");
+  if (env) {
+    const int c = atoi(env);
+    if (c == 1 || c == 2 || c == 4) return c;
+  }
+  int best_c = 1;
+  double best = 1e300;
+  for (int c = 1, lg = 0; c <= 4; c *= 2, ++lg) {
+    const int64_t waves = ((int64_t)heads * c + slots - 1) / slots;
+    const double cost = (double)waves / c * (1.0 + 0.1 * lg);
+    if (cost < best - 1e-9) {
+      best = cost;
+      best_c = c;
+    }
+  }
+  return best_c;
 }
 
 template <bool BF16, typename TI, int DP, int ROWS>
@@ -498,8 +537,26 @@ static cudaError_t launch(const SmallParams& sp, cudaStream_t st) {
   cudaError_t err =
       cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  kfn<<<sp.E * sp.H, kThreads, smem, st>>>(sp);
-  return cudaGetLastError();
+  int dev = 0, sms = 0;
+  err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (err != cudaSuccess) return err;
+  const int heads = sp.E * sp.H;
+  const int csize = cluster_size(heads, sms * (ROWS == 16 ? 4 : 3));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(heads * csize));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kfn, sp);
 }
 
 }  // namespace small
@@ -508,7 +565,7 @@ bool small_supports(const ma_fwd_params* p, const Shape& s) {
   if (p->dtype != MA_DTYPE_BF16 && p->dtype != MA_DTYPE_F16) return false;
   if (s.b > small::kRows || s.M > small::kRows) return false;
   if (s.D != s.Dv || s.D % 8 != 0 || s.D > 128) return false;
-  if ((int64_t)s.E * s.H > 2147483647) return false;
+  if ((int64_t)s.E * s.H * 4 > 2147483647) return false;
   const int64_t* st[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
   for (int t = 0; t < 3; ++t) {  // q / k / v rows read with 16-byte copies
     if (st[t][3] != 1) return false;

@@ -171,6 +171,22 @@ def test_caller_layout_in_and_out(impl, shape, cuda_device):
     assert torch.equal(o_buf.view(E, N, H, D).permute(0, 2, 1, 3), ref)
 
 
+@pytest.mark.parametrize("csize", ["1", "2", "4"])
+def test_small_kernel_cluster_sizes(csize, cuda_device, monkeypatch):
+    """The small-block kernel splits a head over a cluster of 1, 2 or 4 CTAs;
+    every split gives the oracle's result (masked RoBERTa shape, T = 3)."""
+    monkeypatch.setenv("MA_SMALL_CLUSTER", csize)
+    cfg = CONFIGS["roberta_bf16"].with_(E=2, H=2, T=3)
+    q, k, v, mask, _ = make_inputs(cfg, device="cpu")
+    out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                            mask.to(cuda_device), cfg.T, cfg.B, cfg.pre_pad, impl="small")
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    ref = oracle_for(q, k, v, mask, cfg, "f32")
+    err = np.abs(out.float().cpu().numpy() - ref).max()
+    assert err <= tol_for(cfg.dtype, ref), f"cluster {csize}: max|err|={err:.3g}"
+
+
 def test_out_argument_is_checked(cuda_device):
     q = torch.randn(1, 2, 32, 16, device=cuda_device)
     with pytest.raises(ValueError, match="out shape"):
