@@ -18,7 +18,10 @@ The ViT / RoBERTa / BART / DiT hooks call ``attn_module(q, k, v[, mask])`` with
 roberta/model.py:104-106, bart/model.py:150-152,
 dit/attention_processor.py:143); those calls work unchanged.  The work runs
 on the current CUDA stream through ``ma_fwd`` (include/ma_api.h).  Tensors on
-any other device raise: there is no CPU path.
+any other device raise: there is no CPU path.  With inputs that require
+gradients (training, e.g. the BART fine-tuning of the reference) the forward
+still runs on the kernels and the backward recomputes it with autograd
+(``training.py``), as the reference's own training path does.
 """
 from __future__ import annotations
 
@@ -30,7 +33,7 @@ from enum import StrEnum
 import torch
 import torch.nn as nn
 
-from . import _lib
+from . import _lib, training
 
 Tensor = torch.Tensor
 
@@ -163,9 +166,10 @@ def _check_inputs(q: Tensor, k: Tensor, v: Tensor) -> None:
                                f"got a tensor on {t.device}")
     if not (q.device == k.device == v.device):
         raise ValueError("query/key/value are on different devices")
-    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
-        raise RuntimeError("MonarchAttention (B200) implements the forward pass only; "
-                           "call it under torch.no_grad() or torch.inference_mode()")
+
+
+def _needs_grad(q: Tensor, k: Tensor, v: Tensor) -> bool:
+    return torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad)
 
 
 def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int,
@@ -187,6 +191,20 @@ def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None,
     of the (E, N, H*D) projections, no layout copy is made on either side.
     """
     _check_inputs(q, k, v)
+    if _needs_grad(q, k, v):
+        if q.dtype == torch.float8_e4m3fn or scales is not None:
+            raise RuntimeError("gradients through float8 e4m3 inputs are not supported")
+        if out is not None:
+            raise ValueError("out= cannot be used when gradients are required")
+        return training.MonarchAttentionFunction.apply(q, k, v, attn_mask, T, B, pre_pad, impl,
+                                                       _kernel_forward)
+    return _kernel_forward(q, k, v, attn_mask, T, B, pre_pad, impl, scales, out)
+
+
+def _kernel_forward(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int, B: int,
+                    pre_pad: bool, impl=None, scales: tuple | None = None,
+                    out: Tensor | None = None) -> Tensor:
+    """One ``ma_fwd`` call on the current stream (inputs already checked)."""
     E, H, N, _ = q.shape
     Dv = v.shape[-1]
     out_dtype = torch.bfloat16 if q.dtype == torch.float8_e4m3fn else v.dtype
