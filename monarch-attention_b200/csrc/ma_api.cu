@@ -22,6 +22,10 @@ cudaError_t run_small(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
 // ma_convert.cu
 cudaError_t run_e4m3_to_bf16(const ma_fwd_params* p, const Shape& s, void* dq, void* dk, void* dv,
                              cudaStream_t st, int* nlaunch);
+// ma_tc256.cu
+bool tc256_supports(const ma_fwd_params* p, const Shape& s);
+cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
+                      cudaStream_t st, int* nlaunch);
 // ma_tc.cu
 bool tc_supports(const ma_fwd_params* p, const Shape& s);
 size_t tc_ctrl_bytes(const Shape& s);
@@ -163,7 +167,8 @@ int select_impl(const ma_fwd_params* p, const Shape& s, int* impl) {
     vo.out = p->out;
     // (tc_supports checks the output alignment only together with q / k / v)
     const bool out16 = p->out == nullptr || (reinterpret_cast<uintptr_t>(p->out) & 15) == 0;
-    const bool tc = tc_supports(&vo, s) && out16, sm = small_supports(&vo, s);
+    const bool tc = (tc_supports(&vo, s) || tc256_supports(&vo, s)) && out16;
+    const bool sm = small_supports(&vo, s);
     if (p->impl == MA_IMPL_TC && !tc)
       return fail(MA_ERR_UNSUPPORTED, "the tcgen05 kernel does not support this shape");
     if (p->impl == MA_IMPL_SMALL && !sm)
@@ -177,7 +182,7 @@ int select_impl(const ma_fwd_params* p, const Shape& s, int* impl) {
       return MA_OK;
     }
   }
-  const bool tc = tc_supports(p, s);
+  const bool tc = tc_supports(p, s) || tc256_supports(p, s);
   if (p->impl == MA_IMPL_TC) {
     if (!tc) return fail(MA_ERR_UNSUPPORTED, "the tcgen05 kernel does not support this shape");
     *impl = MA_IMPL_TC;
@@ -264,7 +269,8 @@ int ma_fwd(const ma_fwd_params* p, void* stream) {
     err = run_e4m3_to_bf16(p, s, w + ws.xq, w + ws.xk, w + ws.xv, st, &n);
   }
   if (err == cudaSuccess)
-    err = impl == MA_IMPL_TC      ? run_tc(run, s, ws, st, &n)
+    err = impl == MA_IMPL_TC      ? (s.b == 256 ? run_tc256(run, s, ws, st, &n)
+                                                  : run_tc(run, s, ws, st, &n))
           : impl == MA_IMPL_SMALL ? run_small(run, s, ws, st, &n)
                                   : run_generic(run, s, ws, st, &n);
   if (err != cudaSuccess)

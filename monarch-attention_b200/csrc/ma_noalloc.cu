@@ -122,6 +122,10 @@ extern "C" int ma_fwd_noalloc(const ma_fwd_params* p, void* stream) {
     return MA_ERR_NULL_POINTER;
   }
   const ma::Shape s = shape_of(p);
+  if (!ma::tc_supports(p, s)) {  // the b = 256 kernel needs every head's arrays
+    ma::set_error_detail("ma_fwd_noalloc runs the persistent tcgen05 kernel only (block size 64 or 128)");
+    return MA_ERR_UNSUPPORTED;
+  }
   const int nheads = s.E * s.H;
   const int slots = 2 * s.T + 1 < nheads ? 2 * s.T + 1 : nheads;
   size_t status_off = 0;

@@ -1,0 +1,583 @@
+// tcgen05 / TMEM MonarchAttention forward for block size b = number of
+// blocks M = 256 (N = 65536), head dim D = Dv = 128.
+//
+// A reference item (key block m of an R-step, index j of an L / output
+// step) is 256 x 256 here, so a 128-row tile of it has 256 logit columns:
+// GEMM1 is one M = 128, N = 256 MMA chain whose fp32 result fills 256 TMEM
+// columns.  The tile's softmax runs on those columns; its 16-bit P is
+// packed in place into columns 0..127 and GEMM2 (K = 256) writes O into
+// columns 128..255, so one tile needs 256 TMEM columns and two CTAs share
+// an SM.  One launch per phase (the phase boundary is the all-to-all
+// between the (M, b) and (b, M) views), one tile per CTA:
+//
+//   R   (ma_torch.py:10-23; RF adds y, :38-52): rows j of key block m,
+//        softmax over the 256 keys i of the block, al = P K[m], y = P V[m]
+//   LS  (first half of ar_cr_ref, :26-35): rows l of index j, the
+//        log-sum-exp over key blocks k of al_j q_l - cl[k] -> lse[j][l]
+//   LA  (second half): rows k of index j; P^T[k][l] = exp(al_j[k] q_l -
+//        cl[k] - lse[j][l]) are the reference's L[k][l] exactly; cr[k] =
+//        sum_l P^T[k][l], ar[k] = P^T q_j.  The L-step contracts over the
+//        256 query rows l, which a 128-row tile of rows l cannot finish on
+//        its own: the statistics pass makes the L weights column-local.
+//   O   (:55-62): rows l of index j, softmax over k, z = P y_j.
+//
+// Warps 0-3: softmax and epilogue (thread i = TMEM lane = tile row i);
+// warp 4: TMEM allocation, and lane 0 issues every TMA copy and MMA.
+// Every wait is bounded (MA_STATUS_WAIT_TIMEOUT, abort flag); no named
+// barriers; TMA loads without multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "ma_common.cuh"
+#include "ma_tc_ptx.cuh"
+
+namespace ma {
+namespace tc256 {
+
+using namespace ma::tc;
+
+constexpr int kRows = 128;                    // tile rows = TMEM lanes
+constexpr int kCols = 256;                    // logit columns = b = M
+constexpr int kThreads = 160;                 // 4 softmax / epilogue warps + 1 issue warp
+constexpr int kIssueWarp = 4;
+constexpr int kAHalf = kRows * 128;           // 16 KB: 128 rows x 64 columns (SW128)
+constexpr int kABytes = 2 * kAHalf;           // 32 KB
+constexpr int kBHalf = kCols * 128;           // 32 KB: 256 rows x 64 columns
+constexpr int kBBytes = 2 * kBHalf;           // 64 KB
+constexpr uint32_t kTmemCols = 256;
+// small region: barriers, TMEM address, vectors
+constexpr int kOffBar = 0;
+constexpr int kOffTmem = 128;
+constexpr int kOffVecA = 256;                 // per-column vector (cl[k] or lse[l]): 256 fp32
+constexpr int kOffVecB = kOffVecA + 1024;     // per-row vector (cr[j] or cl[k]): 128 fp32
+constexpr int kSmallBytes = kOffVecB + 512;
+constexpr int kSmemBytes = kSmallBytes + 1024 + kABytes + kBBytes;  // + alignment pad
+
+// barriers (8 B each)
+constexpr int kBarFull = 0;     // A, B and the vectors landed
+constexpr int kBarS = 8;        // GEMM1 done (S in TMEM)
+constexpr int kBarP = 16;       // P written to TMEM (128 arrivals)
+constexpr int kBarX = 24;       // late X tile (V or y_j) landed in B
+constexpr int kBarO = 32;       // GEMM2 done (one phase per part)
+constexpr int kBarStaged = 40;  // output tile staged in SMEM (128 arrivals per part)
+constexpr int kBarDrain = 48;   // issued MMAs complete (after an abort)
+
+enum Kind : int { K_R = 0, K_RF = 1, K_LS = 2, K_LA = 3, K_O = 4 };
+
+struct Params {
+  CUtensorMap tm_qblk;   // q (D, N, H, E): 64 x 128 token rows
+  CUtensorMap tm_kblk;
+  CUtensorMap tm_vblk;
+  CUtensorMap tm_qstr;   // q as (D, b, M, H, E): 64 x 1 x 128 -> tokens l*b + j
+  CUtensorMap tm_al;     // al rows [head][j][m]: 64 x 128
+  CUtensorMap tm_ar;     // ar rows [head][m][j]
+  CUtensorMap tm_y;      // y rows  [head][j][m]
+  CUtensorMap tm_al_st;  // al as (D, M, heads*b): 64 x 1 x 128 (rows j of block m)
+  CUtensorMap tm_y_st;
+  CUtensorMap tm_ar_st;  // ar as (D, b, heads*M): rows k of index j
+  CUtensorMap tm_out_st; // out as (Dv, b, M, H, E): tokens l*b + j
+  float* cl;             // [head][j][m]
+  float* cr;             // [head][m][j]
+  float* lse;            // [head][j][l]: log-sum-exp of the L-step rows
+  uint32_t* abort;
+  uint32_t* status;
+  int H;
+  int first;             // R-step of round 0: A = q blocks, cr = 1
+  float sm_scale;
+  unsigned long long timeout_ns;
+};
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// 64 fp32 accumulator columns of this lane -> scaled 16-bit into a 128-row
+// SW128 staging tile (row r of half h at h*16K + r*128, chunk c at c ^ (r & 7))
+template <bool BF16>
+__device__ __forceinline__ void stage_row(uint32_t tile, int row, uint32_t taddr, float scale) {
+#pragma unroll
+  for (int h2 = 0; h2 < 2; ++h2) {
+    uint32_t o[2][32];
+    tmem_ld32(taddr + h2 * 64, o[0]);
+    tmem_ld32(taddr + h2 * 64 + 32, o[1]);
+    tmem_wait_ld();
+    const uint32_t rbase = tile + h2 * kAHalf + row * 128;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint32_t w[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        w[t] = pack2<BF16>(__uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t]) * scale,
+                           __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t + 1]) * scale);
+      st_shared_v4(rbase + ((c ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+template <bool BF16, int KIND>
+__global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t A = (sbase + kSmallBytes + 1023u) & ~1023u;  // SW128 tiles
+  const uint32_t B = A + kABytes;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const Guard guard{p.abort, p.status, p.timeout_ns};
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem_raw + kOffTmem);
+  const float* vecA = reinterpret_cast<const float*>(smem_raw + kOffVecA);
+  const float* vecB = reinterpret_cast<const float*>(smem_raw + kOffVecB);
+  auto bar = [&](int off) { return sbase + kOffBar + off; };
+
+  // tile -> (head, item, row tile)
+  const int tile = blockIdx.x;
+  const int head = tile / (2 * kCols);
+  const int item = (tile >> 1) % kCols;  // m (R steps) or j (L / output)
+  const int rt = tile & 1;                // rows 128*rt .. 128*rt + 127 of the item
+  const int eb = head / p.H, hh = head - eb * p.H;
+  const int hrow = head * kCols;          // first row of this head in [b][M] / [M][b] arrays
+  constexpr bool has_o = KIND != K_LS;
+  constexpr int parts = KIND == K_RF ? 2 : 1;
+
+  if (tid == 0) {
+    mbar_init(bar(kBarFull), 1);
+    mbar_init(bar(kBarS), 1);
+    mbar_init(bar(kBarP), kRows);
+    mbar_init(bar(kBarX), 1);
+    mbar_init(bar(kBarO), 1);
+    mbar_init(bar(kBarStaged), kRows);
+    mbar_init(bar(kBarDrain), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kIssueWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_holder)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+
+  if (warp == kIssueWarp) {
+    if (lane == 0) {
+      const uint64_t keep = policy_evict_last(), once = policy_evict_first();
+      // ---- loads: A (128 rows), B (256 rows), vectors ----
+      const uint32_t fb = bar(kBarFull);
+      uint32_t vbytes = 0;
+      if (KIND == K_R || KIND == K_RF) vbytes = p.first ? 0 : 512;  // cr[m][j-tile]
+      if (KIND == K_LS || KIND == K_O) vbytes = 1024;               // cl[j][:]
+      if (KIND == K_LA) vbytes = 1024 + 512;                        // lse[j][:], cl[j][k-tile]
+      mbar_expect_tx(fb, kABytes + kBBytes + vbytes);
+      const uint32_t va = sbase + kOffVecA, vb = sbase + kOffVecB;
+      if (KIND == K_R || KIND == K_RF) {
+        if (!p.first) bulk_load(vb, p.cr + (size_t)(hrow + item) * kCols + rt * kRows, 512, fb);
+      } else if (KIND == K_LS || KIND == K_O) {
+        bulk_load(va, p.cl + (size_t)(hrow + item) * kCols, 1024, fb);
+      } else {
+        bulk_load(va, p.lse + (size_t)(hrow + item) * kCols, 1024, fb);
+        bulk_load(vb, p.cl + (size_t)(hrow + item) * kCols + rt * kRows, 512, fb);
+      }
+#pragma unroll
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const uint32_t a = A + h2 * kAHalf, b = B + h2 * kBHalf;
+        if (KIND == K_R || KIND == K_RF) {
+          // A: rows j of ar[m] (or of the q block), B: k block m (256 tokens)
+          if (p.first)
+            tma_load_4d_h(a, &p.tm_qblk, h2 * 64, item * kCols + rt * kRows, hh, eb, fb, keep);
+          else
+            tma_load_2d_h(a, &p.tm_ar, h2 * 64, (hrow + item) * kCols + rt * kRows, fb, once);
+          for (int r2 = 0; r2 < 2; ++r2)
+            tma_load_4d_h(b + r2 * kAHalf, &p.tm_kblk, h2 * 64, item * kCols + r2 * kRows, hh,
+                          eb, fb, KIND == K_RF ? once : keep);
+        } else if (KIND == K_LS || KIND == K_O) {
+          // A: q_j rows l (tokens l*b + j), B: al_j (rows k)
+          tma_load_5d_h(a, &p.tm_qstr, h2 * 64, item, rt * kRows, hh, eb, fb, keep);
+          for (int r2 = 0; r2 < 2; ++r2)
+            tma_load_2d_h(b + r2 * kAHalf, &p.tm_al, h2 * 64, (hrow + item) * kCols + r2 * kRows,
+                          fb, KIND == K_O ? once : keep);
+        } else {
+          // A: al_j rows k, B: q_j (all 256 rows l)
+          tma_load_2d_h(a, &p.tm_al, h2 * 64, (hrow + item) * kCols + rt * kRows, fb, once);
+          for (int r2 = 0; r2 < 2; ++r2)
+            tma_load_5d_h(b + r2 * kAHalf, &p.tm_qstr, h2 * 64, item, r2 * kRows, hh, eb, fb,
+                          keep);
+        }
+      }
+      bool ok = wait_bar(fb, 0, guard);
+      // ---- GEMM1: S (128 x 256) = A B^T, both K-major ----
+      if (ok) {
+        tc_fence_after();
+        constexpr uint32_t id1 = idesc_f16(BF16, false, false, kRows, kCols);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t offa = (kk >> 2) * kAHalf + (kk & 3) * 32;
+          const uint32_t offb = (kk >> 2) * kBHalf + (kk & 3) * 32;
+          mma_ss(tmem, smem_desc(A + offa, 16, 1024, kSwz128), smem_desc(B + offb, 16, 1024, kSwz128),
+                 id1, kk > 0);
+        }
+        mma_commit(bar(kBarS));
+      }
+      // out items: y_j replaces al_j in B once GEMM1 has read it
+      if (ok && KIND == K_O) {
+        ok = wait_bar(bar(kBarS), 0, guard);
+        if (ok) {
+          fence_proxy_async_global();
+          mbar_expect_tx(bar(kBarX), kBBytes);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2)
+            for (int r2 = 0; r2 < 2; ++r2)
+              tma_load_2d_h(B + h2 * kBHalf + r2 * kAHalf, &p.tm_y, h2 * 64,
+                            (hrow + item) * kCols + r2 * kRows, bar(kBarX), once);
+        }
+      }
+      // ---- GEMM2 part(s): O (128 x 128) = P (TMEM, K = 256) X (B, MN-major) ----
+      constexpr uint32_t id2 = idesc_f16(BF16, false, true, kRows, 128);
+      for (int part = 0; has_o && ok && part < parts; ++part) {
+        if (part == 0) {
+          ok = wait_bar(bar(kBarP), 0, guard);
+          if (ok && KIND == K_O) ok = wait_bar(bar(kBarX), 0, guard);
+        } else {
+          // R-final: V[m] replaces K[m] once part 0's GEMM2 ran and its O was staged
+          ok = wait_bar(bar(kBarStaged), 0, guard);
+          if (ok) {
+            mbar_expect_tx(bar(kBarX), kBBytes);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2)
+              for (int r2 = 0; r2 < 2; ++r2)
+                tma_load_4d_h(B + h2 * kBHalf + r2 * kAHalf, &p.tm_vblk, h2 * 64,
+                              item * kCols + r2 * kRows, hh, eb, bar(kBarX), once);
+            ok = wait_bar(bar(kBarX), 0, guard);
+          }
+        }
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk)
+          mma_ts(tmem + 128, tmem + kk * 8, smem_desc(B + kk * 2048, kBHalf, 1024, kSwz128), id2,
+                 kk > 0);
+        mma_commit(bar(kBarO));
+        // ---- store the staged output tile ----
+        ok = wait_bar(bar(kBarStaged), part & 1, guard);
+        if (!ok) break;
+        const uint32_t src = part == 0 ? A : B;  // R-final stages y in B (V consumed)
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const uint32_t s2 = src + h2 * kAHalf;
+          if (KIND == K_R || KIND == K_RF)
+            tma_store_3d_h(part == 0 ? &p.tm_al_st : &p.tm_y_st, s2, h2 * 64, item,
+                           hrow + rt * kRows, keep);
+          else if (KIND == K_LA)
+            tma_store_3d_h(&p.tm_ar_st, s2, h2 * 64, item, hrow + rt * kRows, keep);
+          else
+            tma_store_5d_h(&p.tm_out_st, s2, h2 * 64, item, rt * kRows, hh, eb, once);
+        }
+        bulk_commit();
+        bulk_wait_read<0>();
+      }
+      bulk_wait<0>();  // never leave with stores in flight
+      // After an abort, MMAs this thread issued may still run: let them
+      // complete (bounded) before TMEM is released.  (Without an abort the
+      // epilogue has consumed the last one's result.)
+      if (!ok) {
+        mma_commit(bar(kBarDrain));
+        const uint64_t t0 = globaltimer();
+        while (!mbar_try(bar(kBarDrain), 0) && globaltimer() - t0 < guard.limit) {
+        }
+      }
+    }
+  } else {
+    // ===================== softmax + epilogue (warps 0-3) =====================
+    const int row = tid;  // TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off, tO = tS + 128;
+    bool ok = wait_bar_warp(bar(kBarFull), 0, guard) && wait_bar_warp(bar(kBarS), 0, guard);
+    float scale_out = 1.0f;
+    if (ok) {
+      tc_fence_after();
+      // per-row constant (log2 units) and exponent slope
+      float u_a = kLog2e, rowc = 0.0f;
+      if (KIND == K_R || KIND == K_RF) {
+        const float crj = p.first ? 1.0f : vecB[row];
+        u_a = p.sm_scale / (crj + kEps) * kLog2e;  // t = sm_scale * S / (cr + eps) (ma_torch.py:11-12)
+      } else if (KIND == K_LA) {
+        rowc = vecB[row];  // cl[k] of this row
+      }
+      // pass 1: row maximum of the exponent argument (not needed for LA,
+      // whose normaliser lse[l] is known)
+      float mx = 0.0f;
+      if (KIND != K_LA) {
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t sv[64];
+          tmem_ld32(tS + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
+          tmem_ld32(tS + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+          tmem_wait_ld();
+          if (KIND == K_R || KIND == K_RF) {
+#pragma unroll
+            for (int i = 0; i < 64; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[i]));
+          } else {
+            const float4* cv = reinterpret_cast<const float4*>(vecA + 64 * c);
+#pragma unroll
+            for (int i4 = 0; i4 < 16; ++i4) {
+              const float4 c4 = cv[i4];
+              mx4[0] = fmaxf(mx4[0], __uint_as_float(sv[4 * i4]) - c4.x);
+              mx4[1] = fmaxf(mx4[1], __uint_as_float(sv[4 * i4 + 1]) - c4.y);
+              mx4[2] = fmaxf(mx4[2], __uint_as_float(sv[4 * i4 + 2]) - c4.z);
+              mx4[3] = fmaxf(mx4[3], __uint_as_float(sv[4 * i4 + 3]) - c4.w);
+            }
+          }
+        }
+        mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      }
+      // exponent in log2 units: u = u_a * S + u_b - col_k * log2e (columns
+      // subtract cl[k] for LS / O, lse[l] for LA)
+      float u_b;
+      if (KIND == K_R || KIND == K_RF) {
+        const float mxt = fmaxf(u_a * kLn2 * mx, kEps);  // clamp(max, eps) of t (:14-16)
+        u_b = -mxt * kLog2e;
+      } else if (KIND == K_LA) {
+        u_b = -rowc * kLog2e;
+      } else {
+        u_b = -mx * kLog2e;
+      }
+      const bool colsub = KIND != K_R && KIND != K_RF;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f}, w4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[64];
+        tmem_ld32(tS + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
+        tmem_ld32(tS + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+        tmem_wait_ld();
+        const float4* cv = reinterpret_cast<const float4*>(vecA + 64 * c);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          float u = fmaf(__uint_as_float(sv[i]), u_a, u_b);
+          if (colsub) {
+            const float4 c4 = cv[i >> 2];
+            u -= kLog2e * ((i & 3) == 0 ? c4.x : (i & 3) == 1 ? c4.y : (i & 3) == 2 ? c4.z : c4.w);
+          }
+          const float ev = ex2(u);
+          s4[i & 3] += ev;
+          if (KIND == K_R || KIND == K_RF) w4[i & 3] = fmaf(ev, u, w4[i & 3]);
+          sv[i] = __float_as_uint(ev);
+        }
+        if (KIND != K_LS) {
+          // P as packed 16-bit pairs into TMEM columns 32c .. 32c+31: those
+          // S columns were read in this or an earlier chunk
+          uint32_t pk[32];
+#pragma unroll
+          for (int c2 = 0; c2 < 32; ++c2)
+            pk[c2] = pack2<BF16>(__uint_as_float(sv[2 * c2]), __uint_as_float(sv[2 * c2 + 1]));
+          tmem_st32(tS + 32 * c, pk);
+        }
+      }
+      const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+      if (KIND == K_R || KIND == K_RF) {
+        const float wsum = (w4[0] + w4[1]) + (w4[2] + w4[3]);
+        const float den = sum + kEps;  // r = e / (sum + eps), :17
+        const float inv = 1.0f / den;
+        // cl[j][m] = sum_i r_i log r_i (:20); this row is j = 128*rt + row
+        p.cl[(size_t)(hrow + rt * kRows + row) * kCols + item] =
+            kLn2 * inv * wsum - __logf(den) * sum * inv;
+        scale_out = inv;
+      } else if (KIND == K_LS) {
+        // lse[j][l] = max_k x + log(sum_k exp(x - max))
+        p.lse[(size_t)(hrow + item) * kCols + rt * kRows + row] = mx + __logf(sum);
+      } else if (KIND == K_LA) {
+        // cr[k][j] = sum_l L[k][l] (:32); this row is k = 128*rt + row
+        p.cr[(size_t)(hrow + rt * kRows + row) * kCols + item] = sum;
+      } else {
+        scale_out = 1.0f / sum;
+      }
+      if (has_o) {
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar(kBarP));
+      }
+    }
+    // ---- epilogue: O -> scaled 16-bit -> staging tile -> TMA store ----
+    for (int part = 0; has_o && ok && part < parts; ++part) {
+      if (!wait_bar_warp(bar(kBarO), part, guard)) break;
+      tc_fence_after();
+      float sc = scale_out;                                       // z (:60-62), y (:51)
+      if ((KIND == K_R || KIND == K_RF) && part == 0) sc = p.sm_scale * scale_out;  // al (:21)
+      if (KIND == K_LA) sc = 1.0f;                                // ar (:34)
+      stage_row<BF16>(part == 0 ? A : B, row, tO, sc);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar(kBarStaged));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kIssueWarp) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+static bool encode(CUtensorMap* tm, CUtensorMapDataType dt, int rank, const void* base,
+                   const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+  auto fn = get_encode();
+  if (!fn) return false;
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5];
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+  return fn(tm, dt, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bx, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool BF16, int KIND>
+static cudaError_t launch_kind(const Params& prm, int heads, cudaStream_t st) {
+  auto kfn = tc256_kernel<BF16, KIND>;
+  cudaError_t err =
+      cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (err != cudaSuccess) return err;
+  kfn<<<heads * 2 * kCols, kThreads, kSmemBytes, st>>>(prm);
+  return cudaGetLastError();
+}
+
+template <bool BF16>
+static cudaError_t launch(Params& prm, int kind, int heads, cudaStream_t st) {
+  switch (kind) {
+    case K_R: return launch_kind<BF16, K_R>(prm, heads, st);
+    case K_RF: return launch_kind<BF16, K_RF>(prm, heads, st);
+    case K_LS: return launch_kind<BF16, K_LS>(prm, heads, st);
+    case K_LA: return launch_kind<BF16, K_LA>(prm, heads, st);
+    default: return launch_kind<BF16, K_O>(prm, heads, st);
+  }
+}
+
+}  // namespace tc256
+
+static bool aligned16p(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; }
+
+bool tc256_supports(const ma_fwd_params* p, const Shape& s) {
+  const char* off = getenv("MA_DISABLE_TC");
+  if (off && off[0] == '1') return false;
+  if (p->dtype != MA_DTYPE_BF16 && p->dtype != MA_DTYPE_F16) return false;
+  if (s.D != 128 || s.Dv != 128 || s.b != 256 || s.M != 256 || s.N != s.Np) return false;
+  if (p->mask_dtype != MA_MASK_NONE) return false;
+  const int64_t* st[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
+  for (int t = 0; t < 4; ++t) {
+    if (st[t][3] != 1) return false;
+    for (int i = 0; i < 3; ++i)
+      if ((st[t][i] * 2) % 16 != 0 || st[t][i] <= 0) return false;
+  }
+  if (p->q && !(aligned16p(p->q) && aligned16p(p->k) && aligned16p(p->v) && aligned16p(p->out)))
+    return false;
+  return true;
+}
+
+cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, cudaStream_t st,
+                      int* nlaunch) {
+  using namespace tc256;
+  Params prm;
+  memset(&prm, 0, sizeof(prm));
+  const CUtensorMapDataType dt =
+      p->dtype == MA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int heads = s.E * s.H;
+  bool ok = true;
+  const uint32_t box_blk[4] = {64, kRows, 1, 1};
+  auto tok_map = [&](CUtensorMap* tm, const void* base, const int64_t* es) {
+    const uint64_t dims[4] = {(uint64_t)s.D, (uint64_t)s.N, (uint64_t)s.H, (uint64_t)s.E};
+    const uint64_t str[3] = {(uint64_t)es[2] * 2, (uint64_t)es[1] * 2, (uint64_t)es[0] * 2};
+    ok = ok && encode(tm, dt, 4, base, dims, str, box_blk);
+  };
+  tok_map(&prm.tm_qblk, p->q, p->q_stride);
+  tok_map(&prm.tm_kblk, p->k, p->k_stride);
+  tok_map(&prm.tm_vblk, p->v, p->v_stride);
+  {
+    const int64_t* es = p->q_stride;
+    const uint64_t dims[5] = {(uint64_t)s.D, (uint64_t)s.b, (uint64_t)s.M, (uint64_t)s.H,
+                              (uint64_t)s.E};
+    const uint64_t str[4] = {(uint64_t)es[2] * 2, (uint64_t)es[2] * 2 * s.b, (uint64_t)es[1] * 2,
+                             (uint64_t)es[0] * 2};
+    const uint32_t box[5] = {64, 1, kRows, 1, 1};
+    ok = ok && encode(&prm.tm_qstr, dt, 5, p->q, dims, str, box);
+  }
+  char* w = reinterpret_cast<char*>(p->workspace);
+  const uint64_t rows = (uint64_t)heads * s.b * s.M;
+  {
+    const uint64_t dims[2] = {(uint64_t)s.D, rows};
+    const uint64_t str[1] = {(uint64_t)s.D * 2};
+    const uint32_t box[2] = {64, kRows};
+    ok = ok && encode(&prm.tm_al, dt, 2, w + ws.al, dims, str, box);
+    ok = ok && encode(&prm.tm_ar, dt, 2, w + ws.ar, dims, str, box);
+    ok = ok && encode(&prm.tm_y, dt, 2, w + ws.y, dims, str, box);
+  }
+  {
+    const uint32_t box3[3] = {64, 1, kRows};
+    const uint64_t dal[3] = {(uint64_t)s.D, (uint64_t)s.M, (uint64_t)heads * s.b};
+    const uint64_t sal[2] = {(uint64_t)s.D * 2, (uint64_t)s.M * s.D * 2};
+    ok = ok && encode(&prm.tm_al_st, dt, 3, w + ws.al, dal, sal, box3);
+    ok = ok && encode(&prm.tm_y_st, dt, 3, w + ws.y, dal, sal, box3);
+    const uint64_t dar[3] = {(uint64_t)s.D, (uint64_t)s.b, (uint64_t)heads * s.M};
+    const uint64_t sar[2] = {(uint64_t)s.D * 2, (uint64_t)s.b * s.D * 2};
+    ok = ok && encode(&prm.tm_ar_st, dt, 3, w + ws.ar, dar, sar, box3);
+    const int64_t* os = p->o_stride;
+    const uint64_t dout[5] = {(uint64_t)s.Dv, (uint64_t)s.b, (uint64_t)s.M, (uint64_t)s.H,
+                              (uint64_t)s.E};
+    const uint64_t sout[4] = {(uint64_t)os[2] * 2, (uint64_t)os[2] * 2 * s.b,
+                              (uint64_t)os[1] * 2, (uint64_t)os[0] * 2};
+    const uint32_t box5[5] = {64, 1, kRows, 1, 1};
+    ok = ok && encode(&prm.tm_out_st, dt, 5, p->out, dout, sout, box5);
+  }
+  if (!ok) return cudaErrorInvalidValue;
+  prm.cl = reinterpret_cast<float*>(w + ws.cl);
+  prm.cr = reinterpret_cast<float*>(w + ws.cr);
+  prm.lse = reinterpret_cast<float*>(w + ws.lmax);
+  prm.abort = reinterpret_cast<uint32_t*>(w + ws.ctrl) + 1;
+  prm.status = p->status;
+  prm.H = s.H;
+  prm.sm_scale = s.sm_scale;
+  prm.timeout_ns = 2000000000ull;
+  const char* tmo = getenv("MA_WAIT_TIMEOUT_NS");
+  if (tmo) prm.timeout_ns = strtoull(tmo, nullptr, 10);
+  cudaError_t err = cudaMemsetAsync(w + ws.ctrl, 0, 64, st);
+  if (err != cudaSuccess) return err;
+  const bool bf = p->dtype == MA_DTYPE_BF16;
+  auto run = [&](int kind) -> cudaError_t {
+    cudaError_t e = bf ? launch<true>(prm, kind, heads, st) : launch<false>(prm, kind, heads, st);
+    if (e == cudaSuccess) *nlaunch += 1;
+    return e;
+  };
+  // T-1 rounds of (R, L statistics, L accumulation), the final R-step and the output
+  for (int t = 0; t + 1 < s.T && err == cudaSuccess; ++t) {
+    prm.first = t == 0;
+    err = run(K_R);
+    if (err == cudaSuccess) err = run(K_LS);
+    if (err == cudaSuccess) err = run(K_LA);
+  }
+  prm.first = s.T == 1;
+  if (err == cudaSuccess) err = run(K_RF);
+  if (err == cudaSuccess) err = run(K_O);
+  return err;
+}
+
+}  // namespace ma

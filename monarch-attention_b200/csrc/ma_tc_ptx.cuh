@@ -309,7 +309,7 @@ struct Guard {
   }
 };
 
-__device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Guard& g) {
+static __device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Guard& g) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t spin = 1;; ++spin) {
@@ -324,7 +324,7 @@ __device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Guard
   }
 }
 
-__device__ __noinline__ bool wait_counter(const uint32_t* ctr, uint32_t target, const Guard& g) {
+static __device__ __noinline__ bool wait_counter(const uint32_t* ctr, uint32_t target, const Guard& g) {
   if (ld_acquire(ctr) >= target) return true;
   const uint64_t t0 = globaltimer();
   for (;;) {

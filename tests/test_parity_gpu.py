@@ -77,6 +77,7 @@ SMALL = {
     "dit_bf16": dict(E=1, H=2),
     "long4k_bf16": dict(E=1, H=2),
     "long16k_bf16": dict(E=1, H=1),
+    "long64k_bf16": dict(E=1, H=1),
 }
 
 
@@ -108,7 +109,7 @@ def test_config_small(name, impl, cuda_device):
 # full-size configs: every head computed, a sample of heads checked exactly
 # ---------------------------------------------------------------------------
 FULL = ["cfg0_f32", "vit_bf16", "vit_n197_f16", "roberta_bf16", "dit_bf16", "long4k_bf16",
-        "long16k_bf16"]
+        "long16k_bf16", "long64k_bf16"]
 
 
 @pytest.mark.parametrize("name", FULL)
@@ -274,6 +275,7 @@ E4M3_CASES = [("long4k_e4m3", dict(E=1, H=2), "auto"),
               ("long16k_e4m3", dict(E=1, H=1), "auto"),
               ("long16k_e4m3", dict(E=1, H=1), "generic"),
               ("long16k_e4m3", dict(E=1, H=3), "tc"),
+              ("long64k_e4m3", dict(E=1, H=1), "tc"),
               ("vit_bf16", dict(E=2, H=2, dtype="e4m3"), "small"),
               ("roberta_bf16", dict(E=2, H=2, dtype="e4m3"), "small")]
 
@@ -299,6 +301,7 @@ def test_e4m3_routes_to_tensor_core_kernels(cuda_device):
     """e4m3 inputs run on the tensor-core kernels after a bf16 conversion."""
     for name, shape, want in [("long16k_e4m3", dict(E=1, H=1), "tc"),
                               ("long4k_bf16", dict(E=1, H=1), "tc"),
+                              ("long64k_bf16", dict(E=1, H=1), "tc"),
                               ("vit_bf16", dict(E=1, H=1, dtype="e4m3"), "small"),
                               ("long4k_e4m3", dict(E=1, H=1), "tc")]:
         cfg = CONFIGS[name].with_(**shape)
