@@ -63,6 +63,7 @@ constexpr int kBarX = 24;       // late X tile (V or y_j) landed in B
 constexpr int kBarO = 32;       // GEMM2 done (one phase per part)
 constexpr int kBarStaged = 40;  // output tile staged in SMEM (128 arrivals per part)
 constexpr int kBarDrain = 48;   // issued MMAs complete (after an abort)
+constexpr int kBarX2 = 56;      // R-final: V rows 128..255 landed in B
 
 enum Kind : int { K_R = 0, K_RF = 1, K_LS = 2, K_LA = 3, K_O = 4 };
 
@@ -92,17 +93,19 @@ struct Params {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
-// 64 fp32 accumulator columns of this lane -> scaled 16-bit into a 128-row
-// SW128 staging tile (row r of half h at h*16K + r*128, chunk c at c ^ (r & 7))
+// 128 fp32 accumulator columns of this lane -> scaled 16-bit into a 128-row
+// SW128 staging tile (row r of column half h at h*hstride + r*128, chunk c
+// at c ^ (r & 7))
 template <bool BF16>
-__device__ __forceinline__ void stage_row(uint32_t tile, int row, uint32_t taddr, float scale) {
+__device__ __forceinline__ void stage_row(uint32_t tile, uint32_t hstride, int row, uint32_t taddr,
+                                          float scale) {
 #pragma unroll
   for (int h2 = 0; h2 < 2; ++h2) {
     uint32_t o[2][32];
     tmem_ld32(taddr + h2 * 64, o[0]);
     tmem_ld32(taddr + h2 * 64 + 32, o[1]);
     tmem_wait_ld();
-    const uint32_t rbase = tile + h2 * kAHalf + row * 128;
+    const uint32_t rbase = tile + h2 * hstride + row * 128;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint32_t w[4];
@@ -146,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
     mbar_init(bar(kBarO), 1);
     mbar_init(bar(kBarStaged), kRows);
     mbar_init(bar(kBarDrain), 1);
+    mbar_init(bar(kBarX2), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kIssueWarp) {
@@ -219,6 +223,18 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
         }
         mma_commit(bar(kBarS));
       }
+      // R-final items: V rows 0..127 go to A once GEMM1 has read it (rows
+      // 128..255 follow into B after the first GEMM2 part)
+      if (ok && KIND == K_RF) {
+        ok = wait_bar(bar(kBarS), 0, guard);
+        if (ok) {
+          mbar_expect_tx(bar(kBarX), kABytes);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2)
+            tma_load_4d_h(A + h2 * kAHalf, &p.tm_vblk, h2 * 64, item * kCols, hh, eb, bar(kBarX),
+                          once);
+        }
+      }
       // out items: y_j replaces al_j in B once GEMM1 has read it
       if (ok && KIND == K_O) {
         ok = wait_bar(bar(kBarS), 0, guard);
@@ -239,32 +255,48 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
           ok = wait_bar(bar(kBarP), 0, guard);
           if (ok && KIND == K_O) ok = wait_bar(bar(kBarX), 0, guard);
         } else {
-          // R-final: V[m] replaces K[m] once part 0's GEMM2 ran and its O was staged
-          ok = wait_bar(bar(kBarStaged), 0, guard);
-          if (ok) {
-            mbar_expect_tx(bar(kBarX), kBBytes);
-#pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2)
-              for (int r2 = 0; r2 < 2; ++r2)
-                tma_load_4d_h(B + h2 * kBHalf + r2 * kAHalf, &p.tm_vblk, h2 * 64,
-                              item * kCols + r2 * kRows, hh, eb, bar(kBarX), once);
-            ok = wait_bar(bar(kBarX), 0, guard);
-          }
+          // R-final second part: V rows 0..127 in A, rows 128..255 in B
+          ok = wait_bar(bar(kBarX), 0, guard) && wait_bar(bar(kBarX2), 0, guard) &&
+               wait_bar(bar(kBarStaged), 0, guard);  // O of the first part was read
         }
         if (!ok) break;
         tc_fence_after();
+        if (part == 0) {
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk)
-          mma_ts(tmem + 128, tmem + kk * 8, smem_desc(B + kk * 2048, kBHalf, 1024, kSwz128), id2,
-                 kk > 0);
+          for (int kk = 0; kk < 16; ++kk)
+            mma_ts(tmem + 128, tmem + kk * 8, smem_desc(B + kk * 2048, kBHalf, 1024, kSwz128), id2,
+                   kk > 0);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ts(tmem + 128, tmem + kk * 8, smem_desc(A + kk * 2048, kAHalf, 1024, kSwz128), id2,
+                   kk > 0);
+#pragma unroll
+          for (int kk = 8; kk < 16; ++kk)
+            mma_ts(tmem + 128, tmem + kk * 8,
+                   smem_desc(B + kAHalf + (kk - 8) * 2048, kBHalf, 1024, kSwz128), id2, 1);
+        }
         mma_commit(bar(kBarO));
+        if (KIND == K_RF && part == 0) {
+          // V rows 128..255 into the rows 128..255 of B once this GEMM2 has
+          // read K; rows 0..127 of B receive the staged al meanwhile
+          ok = wait_bar(bar(kBarO), 0, guard);
+          if (!ok) break;
+          mbar_expect_tx(bar(kBarX2), kABytes);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2)
+            tma_load_4d_h(B + h2 * kBHalf + kAHalf, &p.tm_vblk, h2 * 64, item * kCols + kRows, hh,
+                          eb, bar(kBarX2), once);
+        }
         // ---- store the staged output tile ----
         ok = wait_bar(bar(kBarStaged), part & 1, guard);
         if (!ok) break;
-        const uint32_t src = part == 0 ? A : B;  // R-final stages y in B (V consumed)
+        // staging: R-final's al in the rows 0..127 of B, everything else in A
+        const bool in_b = KIND == K_RF && part == 0;
+        const uint32_t src = in_b ? B : A, hstride = in_b ? kBHalf : kAHalf;
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
-          const uint32_t s2 = src + h2 * kAHalf;
+          const uint32_t s2 = src + h2 * hstride;
           if (KIND == K_R || KIND == K_RF)
             tma_store_3d_h(part == 0 ? &p.tm_al_st : &p.tm_y_st, s2, h2 * 64, item,
                            hrow + rt * kRows, keep);
@@ -405,7 +437,10 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
       float sc = scale_out;                                       // z (:60-62), y (:51)
       if ((KIND == K_R || KIND == K_RF) && part == 0) sc = p.sm_scale * scale_out;  // al (:21)
       if (KIND == K_LA) sc = 1.0f;                                // ar (:34)
-      stage_row<BF16>(part == 0 ? A : B, row, tO, sc);
+      // R-final: al into the rows 0..127 of B (A holds V rows 0..127 for the
+      // second part), y into A (free once that part ran); else A
+      const bool in_b = KIND == K_RF && part == 0;
+      stage_row<BF16>(in_b ? B : A, in_b ? kBHalf : kAHalf, row, tO, sc);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(bar(kBarStaged));
