@@ -188,6 +188,30 @@ def test_small_kernel_cluster_sizes(csize, cuda_device, monkeypatch):
     assert err <= tol_for(cfg.dtype, ref), f"cluster {csize}: max|err|={err:.3g}"
 
 
+@pytest.mark.parametrize("T,dtype,views", [(1, "bf16", False), (3, "bf16", False),
+                                           (2, "f16", True)])
+def test_block256_kernel_variants(T, dtype, views, cuda_device):
+    """The b = 256 tcgen05 kernel (one launch per phase; L-step split into a
+    log-sum-exp pass and an accumulation pass) for T = 1 (final R-step and
+    output only), T = 3 (two L rounds), fp16, and permuted (E, N, H, D)
+    views in and out; one head against the oracle."""
+    cfg = CONFIGS["long64k_bf16"].with_(E=1, H=1, T=T, dtype=dtype)
+    q, k, v, mask, _ = make_inputs(cfg, device="cpu")
+    dq, dk, dv = (t.to(cuda_device) for t in (q, k, v))
+    out = None
+    if views:
+        E, H, N, D = dq.shape
+        dq, dk, dv = (t.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3) for t in (dq, dk, dv))
+        out = torch.empty(E, N, H, D, dtype=dq.dtype, device=cuda_device).permute(0, 2, 1, 3)
+    assert mab.selected_impl(dq, dk, dv, None, cfg.T, cfg.B, cfg.pre_pad) == "tc"
+    res = monarch_attention(dq, dk, dv, None, cfg.T, cfg.B, cfg.pre_pad, out=out)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    ref = oracle_for(q, k, v, None, cfg, "f32")
+    err = np.abs(res.float().cpu().numpy() - ref).max()
+    assert err <= tol_for(dtype, ref), f"T={T} {dtype}: max|err|={err:.3g}"
+
+
 def test_out_argument_is_checked(cuda_device):
     q = torch.randn(1, 2, 32, 16, device=cuda_device)
     with pytest.raises(ValueError, match="out shape"):
