@@ -63,7 +63,7 @@ typedef enum {
 typedef enum {
   MA_IMPL_AUTO = 0,
   MA_IMPL_GENERIC = 1, /* any shape/dtype: phase kernels, SIMT fp32 math   */
-  MA_IMPL_TC = 2,      /* persistent tcgen05/TMEM kernel (large blocks)     */
+  MA_IMPL_TC = 2,      /* tcgen05/TMEM kernels (b = M in {64, 128, 256})     */
   MA_IMPL_SMALL = 3    /* fused per-head mma.sync kernel (b, M <= 32)       */
 } ma_impl_t;
 
@@ -135,9 +135,10 @@ int ma_fwd(const ma_fwd_params* p, void* stream);
  * array compiled into the library instead of p->workspace, which is ignored.
  * No counterpart in the reference (its PyTorch implementation allocates its
  * intermediates per call, ma/ma_torch.py:89).
- *   - Runs the tcgen05 kernel only: block size = number of blocks = head dim
- *     = 128, bf16 / fp16, no mask; other shapes, and shapes whose scratch
- *     exceeds 64 MiB, return MA_ERR_UNSUPPORTED before anything runs.
+ *   - Runs the persistent tcgen05 kernel only: head dim 128, block size =
+ *     number of blocks = 64 or 128, bf16 / fp16, no mask; other shapes, and
+ *     shapes whose scratch exceeds 64 MiB, return MA_ERR_UNSUPPORTED before
+ *     anything runs.
  *   - Every GPU that loads the library keeps the 64 MiB until process exit.
  *   - All calls on a device share the array: calls that overlap on the GPU
  *     race.  The array keeps the previous call's contents; each call clears

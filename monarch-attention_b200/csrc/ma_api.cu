@@ -1,6 +1,9 @@
 // C ABI of the MonarchAttention forward: argument validation, workspace
-// layout and dispatch between the generic phase kernels and the persistent
-// tcgen05 kernel.  Replaces monarch_attention_torch (ma/ma_torch.py:65-108).
+// layout and dispatch between the kernel families -- the persistent tcgen05
+// kernel (b = 64, 128), the per-phase tcgen05 kernel (b = 256), the fused
+// small-block mma.sync kernel (b, M <= 32) and the generic phase kernels;
+// e4m3 inputs reach the tensor-core ones through a conversion launch.
+// Replaces monarch_attention_torch (ma/ma_torch.py:65-108).
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>

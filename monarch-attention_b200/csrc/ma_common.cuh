@@ -1,5 +1,7 @@
 // Shared device helpers and host-side descriptions for the MonarchAttention
-// kernels (generic phase kernels in ma_generic.cu, tcgen05 kernel in ma_tc.cu).
+// kernels (generic phase kernels in ma_generic.cu, tcgen05 kernels in ma_tc.cu
+// and ma_tc256.cu, small-block kernel in ma_small.cu, e4m3 conversion in
+// ma_convert.cu).
 #pragma once
 
 #include <cuda_bf16.h>

@@ -1,5 +1,6 @@
-// Persistent tcgen05 / TMEM MonarchAttention forward for large blocks
-// (block size b = number of blocks M = head dim = 128, i.e. N = 16384).
+// Persistent tcgen05 / TMEM MonarchAttention forward for large blocks: head
+// dim 128 and block size b = number of blocks M = 128 (N = 16384) or 64
+// (N = 4096, two items per 128-row tile).  b = 256 runs in ma_tc256.cu.
 //
 // Work decomposition.  Per head (e, h) the reference runs 2T phases
 // (ma/ma_torch.py:100-105):
