@@ -212,6 +212,38 @@ def test_block256_kernel_variants(T, dtype, views, cuda_device):
     assert err <= tol_for(dtype, ref), f"T={T} {dtype}: max|err|={err:.3g}"
 
 
+# Shapes the reference accepts that the tensor-core kernels do not take (fp32,
+# a mask, Dv != D, ragged N with front padding, D != 128): the automatic
+# choice must fall back to a kernel that gets them right.
+FALLBACK = [
+    ("f32_b64", dict(E=1, H=1, N=4096, D=128, B=64, T=2, dtype="f32", scaled=False), None),
+    ("mask_b128", dict(E=1, H=1, N=16384, D=128, B=128, T=2, dtype="bf16", scaled=False,
+                       mask_min_len=9000), None),
+    ("dv64_b64", dict(E=1, H=1, N=4096, D=128, B=64, T=2, dtype="bf16", scaled=False, Dv=64), None),
+    ("ragged_prepad_b64", dict(E=1, H=2, N=4000, D=128, B=64, T=2, dtype="bf16", scaled=False,
+                               pre_pad=True), None),
+    ("d64_b64", dict(E=1, H=1, N=4096, D=64, B=64, T=2, dtype="f16"), None),
+]
+
+
+@pytest.mark.parametrize("name,shape,_", FALLBACK, ids=[c[0] for c in FALLBACK])
+def test_shapes_outside_the_tensor_core_kernels(name, shape, _, cuda_device):
+    cfg = CONFIGS["long4k_bf16"].with_(**shape)
+    q, k, v, mask, _s = make_inputs(cfg, device="cpu")
+    assert mab.selected_impl(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                             None if mask is None else mask.to(cuda_device),
+                             cfg.T, cfg.B, cfg.pre_pad) != "tc"
+    out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
+                            None if mask is None else mask.to(cuda_device),
+                            cfg.T, cfg.B, cfg.pre_pad)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert out.shape == (cfg.E, cfg.H, cfg.N, cfg.dv)
+    ref = oracle_for(q, k, v, mask, cfg, "f32")
+    err = np.abs(out.float().cpu().numpy() - ref).max()
+    assert err <= tol_for(cfg.dtype, ref), f"{name}: max|err|={err:.3g}"
+
+
 def test_out_argument_is_checked(cuda_device):
     q = torch.randn(1, 2, 32, 16, device=cuda_device)
     with pytest.raises(ValueError, match="out shape"):
