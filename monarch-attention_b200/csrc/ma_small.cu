@@ -324,7 +324,7 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
       }
     }
 
-    if (PH == PH_L) {
+    if constexpr (PH == PH_L) {
       // cr partial sums and P (16-bit) -> staging tile Pst[l][k]
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -339,9 +339,7 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
           asm volatile("st.shared.b32 [%0], %1;" ::"r"(tP + (r * WT::kPS + c) * 2), "r"(v2)
                        : "memory");
         }
-      continue;
-    }
-
+    } else {
     // ---- R / out: output row tile O = P X over the item's ROWS columns ----
 #pragma unroll 1
     for (int part = 0; part < nparts; ++part) {
@@ -393,6 +391,7 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
         }
       }
     }
+    }  // R / out
   }
 
   if (PH == PH_L) {

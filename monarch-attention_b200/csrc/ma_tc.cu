@@ -131,14 +131,14 @@ struct TcParams {
 enum Kind : int { KIND_R = 0, KIND_L = 1, KIND_O = 2 };
 
 // Optional per-item timeline (compiled in with -DMA_TC_TRACE): for the first
-// kTraceItems items of each CTA, slot 0 holds (head, phase, item) and slots
-// 1..7 globaltimer stamps: 1 claim, 2 dependency met, 3 GEMM1 issued,
-// 4 softmax start, 5 P ready, 6 epilogue start, 7 published; 8.. softmax
-// internals (row 0): 8 late-X issued, 9 pass-1 first TMEM wait, 10 pass 1
-// done, 11 pass-2 first TMEM wait, 12 pass 2 done, 13 pass 3 done,
-// 14 first epilogue TMEM wait, 15 epilogue stores done.
+// kTraceItems items of each CTA, slot 0 holds (head, phase, item) and the
+// other slots globaltimer stamps: 1 claim, 2 dependency met, 3 GEMM1 issued,
+// 4 softmax start, 5 P ready, 6 epilogue start, 15 output staged,
+// 7 published.
+#ifdef MA_TC_TRACE
 constexpr int kTraceItems = 256;
 constexpr int kTraceSlots = 16;
+#endif
 __device__ __forceinline__ void trace_stamp(const TcParams& p, uint32_t n, int slot,
                                             unsigned long long v) {
 #ifdef MA_TC_TRACE
@@ -150,34 +150,7 @@ __device__ __forceinline__ void trace_stamp(const TcParams& p, uint32_t n, int s
 }
 
 
-// convert 32 fp32 accumulator columns * scale to 16-bit and store 64 B
-template <bool BF16>
-__device__ __forceinline__ void store_row32(char* dst, const uint32_t (&o)[32], float scale) {
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t w[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t)
-      w[t] = pack2<BF16>(__uint_as_float(o[c * 8 + 2 * t]) * scale,
-                         __uint_as_float(o[c * 8 + 2 * t + 1]) * scale);
-    st_global_v4(dst + c * 16, w[0], w[1], w[2], w[3]);
-  }
-}
 
-// 128 TMEM accumulator columns of this lane -> scaled 16-bit row of 256 B
-// (64 columns per TMEM round trip)
-template <bool BF16>
-__device__ __forceinline__ void store_row128(char* dst, uint32_t taddr, float scale) {
-#pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    uint32_t o[2][32];
-    tmem_ld32(taddr + h2 * 64, o[0]);
-    tmem_ld32(taddr + h2 * 64 + 32, o[1]);
-    tmem_wait_ld();
-    store_row32<BF16>(dst + h2 * 128, o[0], scale);
-    store_row32<BF16>(dst + h2 * 128 + 64, o[1], scale);
-  }
-}
 
 // 128 TMEM accumulator columns of this lane -> scaled 16-bit row of an output
 // tile staged in SMEM in the SW128 layout the TMA store expects: row r of
