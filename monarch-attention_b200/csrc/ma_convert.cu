@@ -67,6 +67,35 @@ __global__ void __launch_bounds__(kThreads) convert_e4m3_vec16(const ConvParams 
   }
 }
 
+// Row-block path: X / 16 is a power of two dividing the block (D = 128: 8
+// threads per row).  Block (head, row block) converts kRowsPerBlock rows of
+// one (e, h): the head's scale and base pointer are computed once and each
+// thread moves 16 elements per row it visits.
+constexpr int kRowsPerBlock = 256;
+__global__ void __launch_bounds__(kThreads) convert_e4m3_rows(const ConvParams p) {
+  const int t = blockIdx.y;
+  const int X = p.X[t];
+  const int per_row = X >> 4;
+  const int rows_per_step = kThreads / per_row;
+  const int blocks_per_head = (p.N + kRowsPerBlock - 1) / kRowsPerBlock;
+  const int eh = blockIdx.x / blocks_per_head;
+  const int rb = blockIdx.x - eh * blocks_per_head;
+  const int h = eh % p.H, e = eh / p.H;
+  const int64_t* st = p.st[t];
+  const uint8_t* src = p.src[t] + (int64_t)e * st[0] + (int64_t)h * st[1];
+  __nv_bfloat16* dst = p.dst[t] + (size_t)eh * p.N * X;
+  const float sc = p.scale[t][eh];
+  const int c = threadIdx.x % per_row;
+  const int n_end = min(p.N, (rb + 1) * kRowsPerBlock);
+#pragma unroll 2
+  for (int n = rb * kRowsPerBlock + threadIdx.x / per_row; n < n_end; n += rows_per_step) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(src + (int64_t)n * st[2] + c * 16);
+    uint4* dp = reinterpret_cast<uint4*>(dst + (size_t)n * X + c * 16);
+    dp[0] = convert8(raw.x, raw.y, sc);
+    dp[1] = convert8(raw.z, raw.w, sc);
+  }
+}
+
 // Any layout: one element per thread step, 64-bit index math.
 __global__ void __launch_bounds__(kThreads) convert_e4m3_any(const ConvParams p) {
   const int t = blockIdx.y;
@@ -126,10 +155,25 @@ cudaError_t run_e4m3_to_bf16(const ma_fwd_params* p, const Shape& s, void* dq, v
   const int64_t cap = (int64_t)sms * 8;  // grid-stride beyond 8 CTAs per SM
   if (blocks > cap) blocks = cap;
   const dim3 grid((unsigned)blocks, 3);
-  if (vec)
-    conv::convert_e4m3_vec16<<<grid, conv::kThreads, 0, st>>>(cp);
-  else
-    conv::convert_e4m3_any<<<grid, conv::kThreads, 0, st>>>(cp);
+  // row blocks when every tensor's X / 16 is a power of two <= the block
+  bool rows_path = vec;
+  for (int t = 0; t < 3; ++t) {
+    const int pr = X[t] / 16;
+    if (pr < 1 || pr > conv::kThreads || (pr & (pr - 1)) != 0) rows_path = false;
+  }
+  if (rows_path) {
+    const int64_t nblk = (int64_t)s.E * s.H * ((s.N + conv::kRowsPerBlock - 1) / conv::kRowsPerBlock);
+    if (nblk <= 0x7fffffffLL)
+      conv::convert_e4m3_rows<<<dim3((unsigned)nblk, 3), conv::kThreads, 0, st>>>(cp);
+    else
+      rows_path = false;
+  }
+  if (!rows_path) {
+    if (vec)
+      conv::convert_e4m3_vec16<<<grid, conv::kThreads, 0, st>>>(cp);
+    else
+      conv::convert_e4m3_any<<<grid, conv::kThreads, 0, st>>>(cp);
+  }
   err = cudaGetLastError();
   if (err == cudaSuccess) *nlaunch += 1;
   return err;
