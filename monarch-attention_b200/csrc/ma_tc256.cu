@@ -85,6 +85,7 @@ struct Params {
   uint32_t* abort;
   uint32_t* status;
   int H;
+  int heads;             // E * H
   int first;             // R-step of round 0: A = q blocks, cr = 1
   float sm_scale;
   unsigned long long timeout_ns;
@@ -130,16 +131,25 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
   const float* vecA = reinterpret_cast<const float*>(smem_raw + kOffVecA);
   const float* vecB = reinterpret_cast<const float*>(smem_raw + kOffVecB);
   auto bar = [&](int off) { return sbase + kOffBar + off; };
-
-  // tile -> (head, item, row tile)
-  const int tile = blockIdx.x;
-  const int head = tile / (2 * kCols);
-  const int item = (tile >> 1) % kCols;  // m (R steps) or j (L / output)
-  const int rt = tile & 1;                // rows 128*rt .. 128*rt + 127 of the item
-  const int eb = head / p.H, hh = head - eb * p.H;
-  const int hrow = head * kCols;          // first row of this head in [b][M] / [M][b] arrays
   constexpr bool has_o = KIND != K_LS;
   constexpr int parts = KIND == K_RF ? 2 : 1;
+  const int ntiles = p.heads * 2 * kCols;
+
+  // tile -> (head, item, row tile): rows 128*rt .. 128*rt + 127 of item m
+  // (R steps) or j (L / output) of a head
+  struct TileId {
+    int head, item, rt, eb, hh, hrow;
+  };
+  auto tile_id = [&](int t) {
+    TileId d;
+    d.head = t / (2 * kCols);
+    d.item = (t >> 1) % kCols;
+    d.rt = t & 1;
+    d.eb = d.head / p.H;
+    d.hh = d.head - d.eb * p.H;
+    d.hrow = d.head * kCols;  // first row of the head in [b][M] / [M][b] arrays
+    return d;
+  };
 
   if (tid == 0) {
     mbar_init(bar(kBarFull), 1);
@@ -165,157 +175,217 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
   const uint32_t tmem = *tmem_holder;
 
   if (warp == kIssueWarp) {
+    // ===================== TMA + MMA issue (one thread) =====================
+    // The CTA walks its tiles t = blockIdx.x, + gridDim.x, ...  A tile's
+    // loads are issued while the previous tile finishes: B (and the vectors)
+    // as soon as the previous GEMM2 has read B, A once the previous output
+    // store has read its staging in A.
     if (lane == 0) {
       const uint64_t keep = policy_evict_last(), once = policy_evict_first();
-      // ---- loads: A (128 rows), B (256 rows), vectors ----
       const uint32_t fb = bar(kBarFull);
+      const uint32_t va = sbase + kOffVecA, vb = sbase + kOffVecB;
       uint32_t vbytes = 0;
       if (KIND == K_R || KIND == K_RF) vbytes = p.first ? 0 : 512;  // cr[m][j-tile]
       if (KIND == K_LS || KIND == K_O) vbytes = 1024;               // cl[j][:]
       if (KIND == K_LA) vbytes = 1024 + 512;                        // lse[j][:], cl[j][k-tile]
-      mbar_expect_tx(fb, kABytes + kBBytes + vbytes);
-      const uint32_t va = sbase + kOffVecA, vb = sbase + kOffVecB;
-      if (KIND == K_R || KIND == K_RF) {
-        if (!p.first) bulk_load(vb, p.cr + (size_t)(hrow + item) * kCols + rt * kRows, 512, fb);
-      } else if (KIND == K_LS || KIND == K_O) {
-        bulk_load(va, p.cl + (size_t)(hrow + item) * kCols, 1024, fb);
-      } else {
-        bulk_load(va, p.lse + (size_t)(hrow + item) * kCols, 1024, fb);
-        bulk_load(vb, p.cl + (size_t)(hrow + item) * kCols + rt * kRows, 512, fb);
-      }
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        const uint32_t a = A + h2 * kAHalf, b = B + h2 * kBHalf;
+      auto load_vec = [&](const TileId& d) {
         if (KIND == K_R || KIND == K_RF) {
-          // A: rows j of ar[m] (or of the q block), B: k block m (256 tokens)
-          if (p.first)
-            tma_load_4d_h(a, &p.tm_qblk, h2 * 64, item * kCols + rt * kRows, hh, eb, fb, keep);
-          else
-            tma_load_2d_h(a, &p.tm_ar, h2 * 64, (hrow + item) * kCols + rt * kRows, fb, once);
-          for (int r2 = 0; r2 < 2; ++r2)
-            tma_load_4d_h(b + r2 * kAHalf, &p.tm_kblk, h2 * 64, item * kCols + r2 * kRows, hh,
-                          eb, fb, KIND == K_RF ? once : keep);
+          if (!p.first)
+            bulk_load(vb, p.cr + (size_t)(d.hrow + d.item) * kCols + d.rt * kRows, 512, fb);
         } else if (KIND == K_LS || KIND == K_O) {
-          // A: q_j rows l (tokens l*b + j), B: al_j (rows k)
-          tma_load_5d_h(a, &p.tm_qstr, h2 * 64, item, rt * kRows, hh, eb, fb, keep);
-          for (int r2 = 0; r2 < 2; ++r2)
-            tma_load_2d_h(b + r2 * kAHalf, &p.tm_al, h2 * 64, (hrow + item) * kCols + r2 * kRows,
-                          fb, KIND == K_O ? once : keep);
+          bulk_load(va, p.cl + (size_t)(d.hrow + d.item) * kCols, 1024, fb);
         } else {
-          // A: al_j rows k, B: q_j (all 256 rows l)
-          tma_load_2d_h(a, &p.tm_al, h2 * 64, (hrow + item) * kCols + rt * kRows, fb, once);
-          for (int r2 = 0; r2 < 2; ++r2)
-            tma_load_5d_h(b + r2 * kAHalf, &p.tm_qstr, h2 * 64, item, r2 * kRows, hh, eb, fb,
-                          keep);
+          bulk_load(va, p.lse + (size_t)(d.hrow + d.item) * kCols, 1024, fb);
+          bulk_load(vb, p.cl + (size_t)(d.hrow + d.item) * kCols + d.rt * kRows, 512, fb);
         }
+      };
+      auto load_b = [&](const TileId& d) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2)
+          for (int r2 = 0; r2 < 2; ++r2) {
+            const uint32_t dst = B + h2 * kBHalf + r2 * kAHalf;
+            if (KIND == K_R || KIND == K_RF)  // k block m (256 tokens)
+              tma_load_4d_h(dst, &p.tm_kblk, h2 * 64, d.item * kCols + r2 * kRows, d.hh, d.eb, fb,
+                            KIND == K_RF ? once : keep);
+            else if (KIND == K_LS || KIND == K_O)  // al_j (rows k)
+              tma_load_2d_h(dst, &p.tm_al, h2 * 64, (d.hrow + d.item) * kCols + r2 * kRows, fb,
+                            KIND == K_O ? once : keep);
+            else  // q_j (all 256 rows l)
+              tma_load_5d_h(dst, &p.tm_qstr, h2 * 64, d.item, r2 * kRows, d.hh, d.eb, fb, keep);
+          }
+      };
+      auto load_a = [&](const TileId& d) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const uint32_t dst = A + h2 * kAHalf;
+          if (KIND == K_R || KIND == K_RF) {  // rows j of ar[m] (or of the q block)
+            if (p.first)
+              tma_load_4d_h(dst, &p.tm_qblk, h2 * 64, d.item * kCols + d.rt * kRows, d.hh, d.eb,
+                            fb, keep);
+            else
+              tma_load_2d_h(dst, &p.tm_ar, h2 * 64, (d.hrow + d.item) * kCols + d.rt * kRows, fb,
+                            once);
+          } else if (KIND == K_LS || KIND == K_O) {  // q_j rows l (tokens l*b + j)
+            tma_load_5d_h(dst, &p.tm_qstr, h2 * 64, d.item, d.rt * kRows, d.hh, d.eb, fb, keep);
+          } else {  // al_j rows k
+            tma_load_2d_h(dst, &p.tm_al, h2 * 64, (d.hrow + d.item) * kCols + d.rt * kRows, fb,
+                          once);
+          }
+        }
+      };
+      constexpr uint32_t id1 = idesc_f16(BF16, false, false, kRows, kCols);
+      constexpr uint32_t id2 = idesc_f16(BF16, false, true, kRows, 128);
+      bool ok = true;
+      bool pending = false;  // loads of the next tile in flight
+      uint32_t full_phase = 0;
+      int x_it = -1, x2_it = -1;  // tile iterations whose late X / X2 loads were issued
+      int t = blockIdx.x;
+      if (t < ntiles) {
+        const TileId d0 = tile_id(t);
+        mbar_expect_tx(fb, kABytes + kBBytes + vbytes);
+        load_vec(d0);
+        load_b(d0);
+        load_a(d0);
+        pending = true;
       }
-      bool ok = wait_bar(fb, 0, guard);
-      // ---- GEMM1: S (128 x 256) = A B^T, both K-major ----
-      if (ok) {
+      for (int it = 0; ok && t < ntiles; ++it, t += gridDim.x) {
+        const TileId d = tile_id(t);
+        const int tn = t + gridDim.x;
+        const bool has_next = tn < ntiles;
+        const TileId dn = tile_id(has_next ? tn : t);
+        const uint32_t ph = it & 1;
+        ok = wait_bar(fb, full_phase & 1, guard);
+        ++full_phase;
+        pending = false;
+        if (!ok) break;
+        // ---- GEMM1: S (128 x 256) = A B^T, both K-major ----
         tc_fence_after();
-        constexpr uint32_t id1 = idesc_f16(BF16, false, false, kRows, kCols);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t offa = (kk >> 2) * kAHalf + (kk & 3) * 32;
           const uint32_t offb = (kk >> 2) * kBHalf + (kk & 3) * 32;
-          mma_ss(tmem, smem_desc(A + offa, 16, 1024, kSwz128), smem_desc(B + offb, 16, 1024, kSwz128),
-                 id1, kk > 0);
+          mma_ss(tmem, smem_desc(A + offa, 16, 1024, kSwz128),
+                 smem_desc(B + offb, 16, 1024, kSwz128), id1, kk > 0);
         }
         mma_commit(bar(kBarS));
-      }
-      // R-final items: V rows 0..127 go to A once GEMM1 has read it (rows
-      // 128..255 follow into B after the first GEMM2 part)
-      if (ok && KIND == K_RF) {
-        ok = wait_bar(bar(kBarS), 0, guard);
-        if (ok) {
-          mbar_expect_tx(bar(kBarX), kABytes);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2)
-            tma_load_4d_h(A + h2 * kAHalf, &p.tm_vblk, h2 * 64, item * kCols, hh, eb, bar(kBarX),
-                          once);
+        if (KIND == K_LS) {
+          // no GEMM2: A and B are free once GEMM1 ran, the vectors once the
+          // softmax is done with them (and with S)
+          ok = wait_bar(bar(kBarS), ph, guard);
+          if (ok && has_next) {
+            mbar_expect_tx(fb, kABytes + kBBytes + vbytes);
+            load_b(dn);
+            load_a(dn);
+            pending = true;
+          }
+          if (ok) ok = wait_bar(bar(kBarP), ph, guard);
+          if (ok && has_next) load_vec(dn);
+          continue;
         }
-      }
-      // out items: y_j replaces al_j in B once GEMM1 has read it
-      if (ok && KIND == K_O) {
-        ok = wait_bar(bar(kBarS), 0, guard);
-        if (ok) {
-          fence_proxy_async_global();
-          mbar_expect_tx(bar(kBarX), kBBytes);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2)
-            for (int r2 = 0; r2 < 2; ++r2)
-              tma_load_2d_h(B + h2 * kBHalf + r2 * kAHalf, &p.tm_y, h2 * 64,
-                            (hrow + item) * kCols + r2 * kRows, bar(kBarX), once);
-        }
-      }
-      // ---- GEMM2 part(s): O (128 x 128) = P (TMEM, K = 256) X (B, MN-major) ----
-      constexpr uint32_t id2 = idesc_f16(BF16, false, true, kRows, 128);
-      for (int part = 0; has_o && ok && part < parts; ++part) {
-        if (part == 0) {
-          ok = wait_bar(bar(kBarP), 0, guard);
-          if (ok && KIND == K_O) ok = wait_bar(bar(kBarX), 0, guard);
-        } else {
-          // R-final second part: V rows 0..127 in A, rows 128..255 in B
-          ok = wait_bar(bar(kBarX), 0, guard) && wait_bar(bar(kBarX2), 0, guard) &&
-               wait_bar(bar(kBarStaged), 0, guard);  // O of the first part was read
-        }
-        if (!ok) break;
-        tc_fence_after();
-        if (part == 0) {
-#pragma unroll
-          for (int kk = 0; kk < 16; ++kk)
-            mma_ts(tmem + 128, tmem + kk * 8, smem_desc(B + kk * 2048, kBHalf, 1024, kSwz128), id2,
-                   kk > 0);
-        } else {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tmem + 128, tmem + kk * 8, smem_desc(A + kk * 2048, kAHalf, 1024, kSwz128), id2,
-                   kk > 0);
-#pragma unroll
-          for (int kk = 8; kk < 16; ++kk)
-            mma_ts(tmem + 128, tmem + kk * 8,
-                   smem_desc(B + kAHalf + (kk - 8) * 2048, kBHalf, 1024, kSwz128), id2, 1);
-        }
-        mma_commit(bar(kBarO));
-        if (KIND == K_RF && part == 0) {
-          // V rows 128..255 into the rows 128..255 of B once this GEMM2 has
-          // read K; rows 0..127 of B receive the staged al meanwhile
-          ok = wait_bar(bar(kBarO), 0, guard);
+        // R-final: V rows 0..127 to A once GEMM1 has read it; out: y_j to B
+        if (KIND == K_RF || KIND == K_O) {
+          ok = wait_bar(bar(kBarS), ph, guard);
           if (!ok) break;
-          mbar_expect_tx(bar(kBarX2), kABytes);
+          x_it = it;
+          if (KIND == K_RF) {
+            mbar_expect_tx(bar(kBarX), kABytes);
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2)
-            tma_load_4d_h(B + h2 * kBHalf + kAHalf, &p.tm_vblk, h2 * 64, item * kCols + kRows, hh,
-                          eb, bar(kBarX2), once);
-        }
-        // ---- store the staged output tile ----
-        ok = wait_bar(bar(kBarStaged), part & 1, guard);
-        if (!ok) break;
-        // staging: R-final's al in the rows 0..127 of B, everything else in A
-        const bool in_b = KIND == K_RF && part == 0;
-        const uint32_t src = in_b ? B : A, hstride = in_b ? kBHalf : kAHalf;
+            for (int h2 = 0; h2 < 2; ++h2)
+              tma_load_4d_h(A + h2 * kAHalf, &p.tm_vblk, h2 * 64, d.item * kCols, d.hh, d.eb,
+                            bar(kBarX), once);
+          } else {
+            fence_proxy_async_global();
+            mbar_expect_tx(bar(kBarX), kBBytes);
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const uint32_t s2 = src + h2 * hstride;
-          if (KIND == K_R || KIND == K_RF)
-            tma_store_3d_h(part == 0 ? &p.tm_al_st : &p.tm_y_st, s2, h2 * 64, item,
-                           hrow + rt * kRows, keep);
-          else if (KIND == K_LA)
-            tma_store_3d_h(&p.tm_ar_st, s2, h2 * 64, item, hrow + rt * kRows, keep);
-          else
-            tma_store_5d_h(&p.tm_out_st, s2, h2 * 64, item, rt * kRows, hh, eb, once);
+            for (int h2 = 0; h2 < 2; ++h2)
+              for (int r2 = 0; r2 < 2; ++r2)
+                tma_load_2d_h(B + h2 * kBHalf + r2 * kAHalf, &p.tm_y, h2 * 64,
+                              (d.hrow + d.item) * kCols + r2 * kRows, bar(kBarX), once);
+          }
         }
-        bulk_commit();
-        bulk_wait_read<0>();
+        // ---- GEMM2 part(s): O (128 x 128) = P (TMEM, K = 256) X, then store ----
+        for (int part = 0; ok && part < parts; ++part) {
+          const uint32_t ophase = (uint32_t)(it * parts + part) & 1;
+          if (part == 0) {
+            ok = wait_bar(bar(kBarP), ph, guard);
+            if (ok && KIND == K_O) ok = wait_bar(bar(kBarX), ph, guard);
+          } else {
+            // R-final second part: V rows 0..127 in A, rows 128..255 in B
+            ok = wait_bar(bar(kBarX), ph, guard) && wait_bar(bar(kBarX2), ph, guard);
+          }
+          if (!ok) break;
+          tc_fence_after();
+          if (part == 0) {
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk)
+              mma_ts(tmem + 128, tmem + kk * 8, smem_desc(B + kk * 2048, kBHalf, 1024, kSwz128),
+                     id2, kk > 0);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_ts(tmem + 128, tmem + kk * 8, smem_desc(A + kk * 2048, kAHalf, 1024, kSwz128),
+                     id2, kk > 0);
+#pragma unroll
+            for (int kk = 8; kk < 16; ++kk)
+              mma_ts(tmem + 128, tmem + kk * 8,
+                     smem_desc(B + kAHalf + (kk - 8) * 2048, kBHalf, 1024, kSwz128), id2, 1);
+          }
+          mma_commit(bar(kBarO));
+          // this GEMM2 finished reading B: R-final's first part hands rows
+          // 128..255 of B to V; the last part hands B to the next tile
+          ok = wait_bar(bar(kBarO), ophase, guard);
+          if (!ok) break;
+          if (KIND == K_RF && part == 0) {
+            x2_it = it;
+            mbar_expect_tx(bar(kBarX2), kABytes);
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2)
+              tma_load_4d_h(B + h2 * kBHalf + kAHalf, &p.tm_vblk, h2 * 64, d.item * kCols + kRows,
+                            d.hh, d.eb, bar(kBarX2), once);
+          }
+          if (part == parts - 1 && has_next) {
+            mbar_expect_tx(fb, kABytes + kBBytes + vbytes);
+            load_vec(dn);
+            load_b(dn);
+            pending = true;
+          }
+          // ---- store the staged output tile ----
+          ok = wait_bar(bar(kBarStaged), ophase, guard);
+          if (!ok) break;
+          // staging: R-final's al in the rows 0..127 of B, everything else in A
+          const bool in_b = KIND == K_RF && part == 0;
+          const uint32_t src = in_b ? B : A, hstride = in_b ? kBHalf : kAHalf;
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const uint32_t s2 = src + h2 * hstride;
+            if (KIND == K_R || KIND == K_RF)
+              tma_store_3d_h(part == 0 ? &p.tm_al_st : &p.tm_y_st, s2, h2 * 64, d.item,
+                             d.hrow + d.rt * kRows, keep);
+            else if (KIND == K_LA)
+              tma_store_3d_h(&p.tm_ar_st, s2, h2 * 64, d.item, d.hrow + d.rt * kRows, keep);
+            else
+              tma_store_5d_h(&p.tm_out_st, s2, h2 * 64, d.item, d.rt * kRows, d.hh, d.eb, once);
+          }
+          bulk_commit();
+          bulk_wait_read<0>();
+        }
+        if (ok && has_next) load_a(dn);  // the staging in A has been read
       }
       bulk_wait<0>();  // never leave with stores in flight
-      // After an abort, MMAs this thread issued may still run: let them
-      // complete (bounded) before TMEM is released.  (Without an abort the
-      // epilogue has consumed the last one's result.)
       if (!ok) {
-        mma_commit(bar(kBarDrain));
+        // After an abort: loads of the next tile may be in flight, and MMAs
+        // this thread issued may still run; let both finish (bounded)
+        // before the CTA releases shared memory and TMEM.
         const uint64_t t0 = globaltimer();
-        while (!mbar_try(bar(kBarDrain), 0) && globaltimer() - t0 < guard.limit) {
+        while (pending && !mbar_try(fb, full_phase & 1) && globaltimer() - t0 < guard.limit) {
+        }
+        while (x_it >= 0 && !mbar_try(bar(kBarX), x_it & 1) && globaltimer() - t0 < guard.limit) {
+        }
+        while (x2_it >= 0 && !mbar_try(bar(kBarX2), x2_it & 1) && globaltimer() - t0 < guard.limit) {
+        }
+        mma_commit(bar(kBarDrain));
+        const uint64_t t1 = globaltimer();
+        while (!mbar_try(bar(kBarDrain), 0) && globaltimer() - t1 < guard.limit) {
         }
       }
     }
@@ -324,10 +394,14 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
     const int row = tid;  // TMEM lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + lane_off, tO = tS + 128;
-    bool ok = wait_bar_warp(bar(kBarFull), 0, guard) && wait_bar_warp(bar(kBarS), 0, guard);
-    float scale_out = 1.0f;
-    if (ok) {
+    bool ok = true;
+    for (int it = 0, t = blockIdx.x; ok && t < ntiles; ++it, t += gridDim.x) {
+      const TileId d = tile_id(t);
+      const uint32_t ph = it & 1;
+      ok = wait_bar_warp(bar(kBarFull), ph, guard) && wait_bar_warp(bar(kBarS), ph, guard);
+      if (!ok) break;
       tc_fence_after();
+      float scale_out = 1.0f;
       // per-row constant (log2 units) and exponent slope
       float u_a = kLog2e, rowc = 0.0f;
       if (KIND == K_R || KIND == K_RF) {
@@ -412,38 +486,41 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
         const float den = sum + kEps;  // r = e / (sum + eps), :17
         const float inv = 1.0f / den;
         // cl[j][m] = sum_i r_i log r_i (:20); this row is j = 128*rt + row
-        p.cl[(size_t)(hrow + rt * kRows + row) * kCols + item] =
+        p.cl[(size_t)(d.hrow + d.rt * kRows + row) * kCols + d.item] =
             kLn2 * inv * wsum - __logf(den) * sum * inv;
         scale_out = inv;
       } else if (KIND == K_LS) {
         // lse[j][l] = max_k x + log(sum_k exp(x - max))
-        p.lse[(size_t)(hrow + item) * kCols + rt * kRows + row] = mx + __logf(sum);
+        p.lse[(size_t)(d.hrow + d.item) * kCols + d.rt * kRows + row] = mx + __logf(sum);
       } else if (KIND == K_LA) {
         // cr[k][j] = sum_l L[k][l] (:32); this row is k = 128*rt + row
-        p.cr[(size_t)(hrow + rt * kRows + row) * kCols + item] = sum;
+        p.cr[(size_t)(d.hrow + d.rt * kRows + row) * kCols + d.item] = sum;
       } else {
         scale_out = 1.0f / sum;
       }
-      if (has_o) {
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(bar(kBarP));
-      }
-    }
-    // ---- epilogue: O -> scaled 16-bit -> staging tile -> TMA store ----
-    for (int part = 0; has_o && ok && part < parts; ++part) {
-      if (!wait_bar_warp(bar(kBarO), part, guard)) break;
-      tc_fence_after();
-      float sc = scale_out;                                       // z (:60-62), y (:51)
-      if ((KIND == K_R || KIND == K_RF) && part == 0) sc = p.sm_scale * scale_out;  // al (:21)
-      if (KIND == K_LA) sc = 1.0f;                                // ar (:34)
-      // R-final: al into the rows 0..127 of B (A holds V rows 0..127 for the
-      // second part), y into A (free once that part ran); else A
-      const bool in_b = KIND == K_RF && part == 0;
-      stage_row<BF16>(in_b ? B : A, in_b ? kBHalf : kAHalf, row, tO, sc);
-      fence_proxy_async_smem();
+      // P written (TMEM), S and the vectors no longer read
+      if (has_o) tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(kBarStaged));
+      mbar_arrive(bar(kBarP));
+      // ---- epilogue: O -> scaled 16-bit -> staging tile -> TMA store ----
+      for (int part = 0; has_o && part < parts; ++part) {
+        const uint32_t ophase = (uint32_t)(it * parts + part) & 1;
+        if (!wait_bar_warp(bar(kBarO), ophase, guard)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float sc = scale_out;                                       // z (:60-62), y (:51)
+        if ((KIND == K_R || KIND == K_RF) && part == 0) sc = p.sm_scale * scale_out;  // al (:21)
+        if (KIND == K_LA) sc = 1.0f;                                // ar (:34)
+        // R-final: al into the rows 0..127 of B (A holds V rows 0..127 for
+        // the second part), y into A (free once that part ran); else A
+        const bool in_b = KIND == K_RF && part == 0;
+        stage_row<BF16>(in_b ? B : A, in_b ? kBHalf : kAHalf, row, tO, sc);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(bar(kBarStaged));
+      }
     }
   }
 
@@ -493,7 +570,14 @@ static cudaError_t launch_kind(const Params& prm, int heads, cudaStream_t st) {
   cudaError_t err =
       cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (err != cudaSuccess) return err;
-  kfn<<<heads * 2 * kCols, kThreads, kSmemBytes, st>>>(prm);
+  int dev = 0, sms = 0;
+  err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (err != cudaSuccess) return err;
+  const int64_t tiles = (int64_t)heads * 2 * kCols;
+  const int grid = (int)(tiles < 2LL * sms ? tiles : 2LL * sms);  // two resident CTAs per SM
+  kfn<<<grid, kThreads, kSmemBytes, st>>>(prm);
   return cudaGetLastError();
 }
 
@@ -590,6 +674,7 @@ cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
   prm.abort = reinterpret_cast<uint32_t*>(w + ws.ctrl) + 1;
   prm.status = p->status;
   prm.H = s.H;
+  prm.heads = heads;
   prm.sm_scale = s.sm_scale;
   prm.timeout_ns = 2000000000ull;
   const char* tmo = getenv("MA_WAIT_TIMEOUT_NS");
