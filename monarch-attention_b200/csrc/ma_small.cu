@@ -105,6 +105,14 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return r;
 }
 
+constexpr float kLog2eS = 1.4426950408889634f;
+constexpr float kLn2S = 0.6931471805599453f;
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ bool token_valid(const SmallParams& p, int e, int pidx) {
   const int n = pidx - p.pad_off;
   if (n < 0 || n >= p.N) return false;
@@ -218,15 +226,20 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
   // output (rows k of P^T Q_j) one 16-row tile at a time.
   const int g = lane >> 2, t4 = lane & 3;
   bool colv[NT][2];
-  float colc[NT][2];  // per-column term: cl[j][k] (L / out)
+  float colc[NT][2];  // per-column term in log2 units: cl[j][k] * log2(e) (L / out)
+  bool allv = true;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const int c = nt * 8 + 2 * t4 + q;
       colv[nt][q] = c < C && (!rph || valid_bit(vbits, item * b + c));
-      colc[nt][q] = (!rph && c < C) ? vec[c] : 0.0f;
+      colc[nt][q] = (!rph && c < C) ? vec[c] * kLog2eS : 0.0f;
+      allv = allv && colv[nt][q];
     }
+  // every column of the item valid (no padding, no masked key): the
+  // softmax below skips its masking selects
+  allv = __all_sync(0xffffffffu, allv);
   float colsum[NT][2];  // L-step: column sums of P over the rows (cr)
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) colsum[nt][0] = colsum[nt][1] = 0.0f;
@@ -260,6 +273,10 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
     }
     // ---- softmax over the columns of each row ----
     // fragment element (nt, i): row mt*16 + g + 8*(i>>1), col nt*8 + 2*t4 + (i&1)
+    // Exponents in log2 units, u = ua * x + ub (- colc for L / out): one FMA
+    // and one ex2 per element.  R and out rows keep e unnormalised; their
+    // 1 / sum goes into the output scale (row_scale), as the second matmul
+    // is linear in the rows of P.
     float row_scale[2], cl_row[2];
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
@@ -267,31 +284,40 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
       float c = 1.0f;
       if (rph) {
         const float crj = (first || r >= R) ? 1.0f : vec[r];
-        c = p.sm_scale / (crj + kEps);  // ma_torch.py:11-12
+        c = p.sm_scale / (crj + kEps);  // t = sm_scale * S / (cr + eps), ma_torch.py:11-12
       }
+      // pass 1: row maximum (R: of S, as c > 0 gives max t = c * max S)
       float mx = -INFINITY;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
-          float& x = acc[nt][2 * hf + q];
-          x = rph ? x * c : x - colc[nt][q];
-          if (!colv[nt][q]) x = -INFINITY;
+          float x = acc[nt][2 * hf + q];
+          if (!rph) x -= colc[nt][q] * kLn2S;
+          if (!allv && !colv[nt][q]) x = -INFINITY;
           mx = fmaxf(mx, x);
         }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      if (rph) mx = fmaxf(mx, kEps);  // clamp(max, min=eps), :14-16
+      float ua, ub;
+      if (rph) {
+        ua = c * kLog2eS;
+        ub = -fmaxf(c * mx, kEps) * kLog2eS;  // clamp(max t, min=eps), :14-16
+      } else {
+        ua = kLog2eS;
+        ub = -mx * kLog2eS;
+      }
       float sum = 0.0f, wsum = 0.0f;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           float& x = acc[nt][2 * hf + q];
-          const float tt = x - mx;
-          const float ev = colv[nt][q] ? __expf(tt) : 0.0f;
+          const float u = fmaf(x, ua, rph ? ub : ub - colc[nt][q]);
+          float ev = ex2f(u);
+          if (!allv && !colv[nt][q]) ev = 0.0f;
           sum += ev;
-          if (rph && colv[nt][q]) wsum = fmaf(ev, tt, wsum);
+          if (rph) wsum = fmaf(ev, (allv || colv[nt][q]) ? u : 0.0f, wsum);
           x = ev;
         }
       sum += __shfl_xor_sync(0xffffffffu, sum, 1);
@@ -299,22 +325,26 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
       if (rph) {
         wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
         wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
-        const float den = sum + kEps;  // :17
+        const float den = sum + kEps;  // r = e / (sum + eps), :17
         const float inv = 1.0f / den;
-        cl_row[hf] = inv * wsum - __logf(den) * sum * inv;  // sum r log r, :20
+        // sum_i r_i log r_i, log r_i = ln2 * u_i - log(den) (:20)
+        cl_row[hf] = kLn2S * inv * wsum - __logf(den) * sum * inv;
         row_scale[hf] = inv;
       } else {
         cl_row[hf] = 0.0f;
         row_scale[hf] = 1.0f / sum;
       }
-      // normalised probabilities (the reference rounds r / l to the input dtype
-      // before its second matmul); L-step: times the query mask of row l (:30)
-      float sc = row_scale[hf];
-      if (PH == PH_L && !(r < R && valid_bit(vbits, r * b + item))) sc = 0.0f;
+      if (PH == PH_L) {
+        // the L-step's P is normalised here (its column sums are cr, and its
+        // transpose is the second matmul's operand), times the query mask of
+        // row l (:30)
+        float sc = row_scale[hf];
+        if (!(r < R && valid_bit(vbits, r * b + item))) sc = 0.0f;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
+        for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int q = 0; q < 2; ++q) acc[nt][2 * hf + q] *= sc;
+          for (int q = 0; q < 2; ++q) acc[nt][2 * hf + q] *= sc;
+      }
     }
     if (rph) {  // cl[j][m] (:20)
 #pragma unroll
@@ -370,10 +400,10 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
         const int r = mt * 16 + g + 8 * hf;
         if (r >= R) continue;
         char* dst;
-        float sc = 1.0f;
+        float sc = row_scale[hf];  // 1 / (sum + eps) of R rows, 1 / sum of out rows
         if (rph && part == 0) {  // al[j][m] = sm_scale * (r K[m])  (:21)
           dst = p.al + ((size_t)eh * b * M + (size_t)r * M + item) * D * esz;
-          sc = p.sm_scale;
+          sc *= p.sm_scale;
         } else if (rph) {        // y[j][m] = r V[m] (:51)
           dst = p.y + ((size_t)eh * b * M + (size_t)r * M + item) * D * esz;
         } else {                 // z at token l*b + j (:60-62, :106-108)
