@@ -21,13 +21,17 @@
 // the output phase of the head that used it before), so the live set stays
 // L2-resident.
 //
-// CTA roles (384 threads = 3 warpgroups, one CTA per SM):
-//   warpgroups 0, 1  softmax + epilogue; group g takes the items n with
-//                    n % 2 == g (ping-pong), thread i owns row i = TMEM lane i
-//   warp 8           scheduler + TMA producer (3-entry ring, 2 tiles each)
-//   warp 9           TMEM allocator + tcgen05.mma issuer
-// The softmax streams each row out of TMEM in 64-column halves, so every
-// thread fits in the 168 registers a 384-thread CTA gets.
+// CTA roles (512 threads, one CTA per SM):
+//   warpgroups 0, 1  softmax; group g takes the items n with n % 2 == g
+//                    (ping-pong), thread i owns row i = TMEM lane i
+//   warpgroup 2      epilogue (O -> 16-bit staging in shared memory)
+//   warp 12          scheduler + TMA producer (3-entry ring, 2 tiles each)
+//   warp 13          TMEM allocator + tcgen05.mma issuer
+//   warps 14, 15     TMA stores + publication of alternate items
+// The softmax and the epilogue stream each row out of TMEM in 16-column
+// chunks, the next chunk's load in flight while the current one is
+// processed, in small loop bodies with few live registers (the whole CTA
+// gets 128 registers per thread).
 // Per item n (group g = n % 2, ring entry e = n % 3):
 //   GEMM1  S[g] = A * B^T        (A, B: K-major SW128 tiles of entry e)
 //   softmax over the row (fp32, exp2); P -> TMEM S[g] as 16-bit (R / out
@@ -123,10 +127,12 @@ struct TcParams {
   int H, nheads, T, P, slots;
   int hgroup;  // heads per wavefront phase slot (round r runs phase p of heads hgroup*(r-p) + i)
   int early;   // 1: claim the next item (and await its dependency) before its ring entry frees
+  int claim;   // items claimed per global atomic
   float sm_scale;
   unsigned long long timeout_ns;
   unsigned long long* trace;  // MA_TC_TRACE builds: per-CTA item timestamps, else null
 };
+
 
 enum Kind : int { KIND_R = 0, KIND_L = 1, KIND_O = 2 };
 
@@ -154,25 +160,34 @@ __device__ __forceinline__ void trace_stamp(const TcParams& p, uint32_t n, int s
 
 // 128 TMEM accumulator columns of this lane -> scaled 16-bit row of an output
 // tile staged in SMEM in the SW128 layout the TMA store expects: row r of
-// half h at h*16K + r*128, 16-byte chunk c at position c ^ (r & 7)
+// half h at h*16K + r*128, 16-byte unit c at position c ^ (r & 7).  The row
+// is read in 16-column chunks with the next chunk's load in flight.
 template <bool BF16>
 __device__ __forceinline__ void stage_row128(uint32_t tile, int row, uint32_t taddr, float scale) {
+  uint32_t ca[16], cb[16];
+  const uint32_t rbase = tile + row * 128;
+  auto put = [&](const uint32_t(&cv)[16], int ch) {
 #pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    uint32_t o[2][32];
-    tmem_ld32(taddr + h2 * 64, o[0]);
-    tmem_ld32(taddr + h2 * 64 + 32, o[1]);
-    tmem_wait_ld();
-    const uint32_t rbase = tile + h2 * kHalf + row * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int t = 0; t < 2; ++t) {
       uint32_t w[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
-        w[t] = pack2<BF16>(__uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t]) * scale,
-                           __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t + 1]) * scale);
-      st_shared_v4(rbase + ((c ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
+      for (int q = 0; q < 4; ++q)
+        w[q] = pack2<BF16>(__uint_as_float(cv[8 * t + 2 * q]) * scale,
+                           __uint_as_float(cv[8 * t + 2 * q + 1]) * scale);
+      const int u = 2 * ch + t;
+      st_shared_v4(rbase + (u >> 3) * kHalf + (((u & 7) ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
     }
+  };
+  tmem_ld16(taddr, ca);
+  tmem_wait_ld();
+#pragma unroll 1
+  for (int ch = 0; ch < 8; ch += 2) {
+    tmem_ld16(taddr + 16 * (ch + 1), cb);
+    put(ca, ch);
+    tmem_wait_ld();
+    if (ch + 2 < 8) tmem_ld16(taddr + 16 * (ch + 2), ca);
+    put(cb, ch + 1);
+    tmem_wait_ld();
   }
 }
 
@@ -274,6 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       uint32_t blk = 0;
       uint32_t issued = 0;  // bit e: a load was issued on entry e
       uint32_t last_on[kEntries] = {0, 0, 0};
+      // Items are claimed p.claim at a time (one global atomic per batch), and
+      // the last (head, phase) whose dependency was seen complete is
+      // remembered (completion is final), so consecutive items of one
+      // (head, phase) block cost no global round trip at all.
+      uint32_t w_next = 0, w_end = 0;
+      int dep_head = -1, dep_ph = -1;
       uint32_t n = 0;
       for (;; ++n) {
         const int e = n % kEntries;
@@ -282,7 +303,11 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         if (!p.early && n >= kEntries && !wait_bar(bar(kBarEmpty, e), (use - 1) & 1, guard))
           break;
         trace_stamp(p, n, 1, globaltimer());
-        const uint32_t w = atomicAdd(ctrl + kCtrlNext, 1u);
+        if (w_next == w_end) {
+          w_next = atomicAdd(ctrl + kCtrlNext, (uint32_t)p.claim);
+          w_end = w_next + (uint32_t)p.claim;
+        }
+        const uint32_t w = w_next++;
         bool ok = w < total && !ld_relaxed(guard.abort);
         int head = -1, item = 0, kind = 0;
         if (ok) {
@@ -310,11 +335,17 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           kind = (ph & 1) == 0 ? KIND_R : (ph == P - 1 ? KIND_O : KIND_L);
           // dependency: the previous phase of this head, or -- for phase 0 --
           // the output phase of the head that used this workspace slot before
-          if (ph > 0)
-            ok = wait_counter(ctrl + kCtrlDone + head * P + ph - 1, (uint32_t)kTiles, guard);
-          else if (head >= p.slots)
-            ok = wait_counter(ctrl + kCtrlDone + (head - p.slots) * P + P - 1, (uint32_t)kTiles,
-                              guard);
+          if (head != dep_head || ph != dep_ph) {
+            if (ph > 0)
+              ok = wait_counter(ctrl + kCtrlDone + head * P + ph - 1, (uint32_t)kTiles, guard);
+            else if (head >= p.slots)
+              ok = wait_counter(ctrl + kCtrlDone + (head - p.slots) * P + P - 1, (uint32_t)kTiles,
+                                guard);
+            if (ok) {
+              dep_head = head;
+              dep_ph = ph;
+            }
+          }
         }
         if (p.early && n >= kEntries && !wait_bar(bar(kBarEmpty, e), (use - 1) & 1, guard))
           break;
@@ -564,31 +595,39 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           discard_l2(reinterpret_cast<const char*>((kind == KIND_R ? p.cr : p.cl) + trow) + row * 128);
       }
 
-      // The row of S (128 fp32) is streamed out of TMEM in 64-column halves:
-      // pass 1 takes the row maximum, pass 2 exponentiates and sums (P goes
-      // back to TMEM; for L items e goes back in place), pass 3 (L only)
-      // normalises and writes P^T to shared memory.
+      // The row of S (128 fp32) is streamed out of TMEM in 16-column chunks,
+      // the next chunk's load in flight while the current one is processed
+      // (small loop bodies, few live registers): pass 1 takes the row
+      // maximum, pass 2 exponentiates and sums (P goes back to TMEM; for L
+      // items e goes back in place), pass 3 (L only) normalises and writes
+      // P^T to shared memory.  Chunks c_lo .. c_hi - 1 (an even count) are
+      // this row's columns 16 c ..
+      const int c_lo = 4 * h_lo, c_hi = 4 * h_hi;
       const bool rk = kind == KIND_R;
       float c = 1.0f;  // R: sm_scale / (cr_j + eps)
       if (rk) c = p.sm_scale / ((ph > 0 ? vec[row] : 1.0f) + kEps);
+      uint32_t ca[16], cb[16];
       float mx;
       {
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-        for (int h2 = h_lo; h2 < h_hi; ++h2) {
-          uint32_t sv[64];
-          tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
-          tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-          tmem_wait_ld();
+        auto max_chunk = [&](const uint32_t(&cv)[16], int ch) {
           if (rk) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[i]));
+            for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(cv[i]));
           } else {
-            const float* cv = vec + 64 * h2;
+            const float* vv = vec + 16 * ch;
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[i]) - cv[i]);
+            for (int i = 0; i < 16; ++i)
+              mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(cv[i]) - vv[i]);
           }
+        };
+#pragma unroll 1
+        for (int ch = c_lo; ch < c_hi; ch += 2) {  // the maximum needs no prefetch
+          tmem_ld16(tS + 16 * ch, ca);
+          tmem_ld16(tS + 16 * (ch + 1), cb);
+          tmem_wait_ld();
+          max_chunk(ca, ch);
+          max_chunk(cb, ch + 1);
         }
         mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
@@ -604,33 +643,48 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         u_b = -mx * kLog2e;
       }
       float s4[4] = {0.f, 0.f, 0.f, 0.f}, w4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int h2 = h_lo; h2 < h_hi; ++h2) {
-        uint32_t sv[64];
-        tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      uint64_t s2[2] = {0ull, 0ull}, w2[2] = {0ull, 0ull};
+      const uint64_t ua2 = f2pack(u_a, u_a), ub2 = f2pack(u_b, u_b);
+      {
+        // e of chunk ch; back to TMEM as fp32 in place (L) or as packed
+        // 16-bit pairs into columns 8 ch .. 8 ch + 7 (R / out: those S
+        // columns were read already, and the chunk in flight lies beyond)
+        auto exp_chunk = [&](uint32_t(&cv)[16], int ch) {
+          const uint64_t* vv = reinterpret_cast<const uint64_t*>(vec + 16 * ch);
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            uint64_t x2 = f2pack(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1]));
+            if (!rk) x2 = fsub2(x2, vv[t]);
+            const uint64_t u2 = ffma2(x2, ua2, ub2);
+            float u0, u1;
+            f2unpack(u2, u0, u1);
+            const float e0 = ex2(u0), e1 = ex2(u1);
+            const uint64_t e2 = f2pack(e0, e1);
+            s2[t & 1] = fadd2(s2[t & 1], e2);
+            if (rk) w2[t & 1] = ffma2(e2, u2, w2[t & 1]);
+            cv[2 * t] = __float_as_uint(e0);
+            cv[2 * t + 1] = __float_as_uint(e1);
+          }
+          if (kind == KIND_L) {
+            tmem_st16(tS + 16 * ch, cv);
+          } else {
+            uint32_t pk[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              pk[t] = pack2<BF16>(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1]));
+            tmem_st8(tS + 8 * ch, pk);
+          }
+        };
+        tmem_ld16(tS + 16 * c_lo, ca);
         tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          float x = __uint_as_float(sv[i]);
-          if (!rk) x -= vec[64 * h2 + i];
-          const float u = fmaf(x, u_a, u_b);
-          const float ev = ex2(u);
-          s4[i & 3] += ev;
-          if (rk) w4[i & 3] = fmaf(ev, u, w4[i & 3]);
-          sv[i] = __float_as_uint(ev);
-        }
-        if (kind == KIND_L) {  // e back in place (fp32), normalised in pass 3
-          tmem_st32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
-          tmem_st32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        } else {
-          // P (unnormalised) as packed 16-bit pairs into TMEM columns
-          // 32*h2 .. 32*h2+31: those S columns were already read
-          uint32_t pk[32];
-#pragma unroll
-          for (int c2 = 0; c2 < 32; ++c2)
-            pk[c2] = pack2<BF16>(__uint_as_float(sv[2 * c2]), __uint_as_float(sv[2 * c2 + 1]));
-          tmem_st32(tS + 32 * h2, pk);
+#pragma unroll 1
+        for (int ch = c_lo; ch < c_hi; ch += 2) {
+          tmem_ld16(tS + 16 * (ch + 1), cb);
+          exp_chunk(ca, ch);
+          tmem_wait_ld();
+          if (ch + 2 < c_hi) tmem_ld16(tS + 16 * (ch + 2), ca);
+          exp_chunk(cb, ch + 1);
+          tmem_wait_ld();
         }
       }
       if (PACK == 2 && kind != KIND_L) {  // P of the other item's block is zero
@@ -640,6 +694,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         tmem_st32(tS + 32 * (1 - pk_row), z);
       }
       tmem_wait_st();
+      f2unpack(s2[0], s4[0], s4[1]);
+      f2unpack(s2[1], s4[2], s4[3]);
+      f2unpack(w2[0], w4[0], w4[1]);
+      f2unpack(w2[1], w4[2], w4[3]);
       const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       float scale_out;
       if (rk) {
@@ -666,21 +724,32 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           for (int cc = 0; cc < 8; ++cc)
             st_shared_v4(prow + (1 - pk_row) * kHalf + ((cc ^ (row & 7)) << 4), 0u, 0u, 0u, 0u);
         }
-#pragma unroll 1
-        for (int h2 = h_lo; h2 < h_hi; ++h2) {
-          uint32_t sv[64];
-          tmem_ld32(tS + 64 * h2, *reinterpret_cast<uint32_t(*)[32]>(sv));
-          tmem_ld32(tS + 64 * h2 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-          tmem_wait_ld();
+        // chunk ch = two 16-byte units (8 columns each) of the row: unit
+        // u = 2 ch + t of the 128-column row sits in half u / 8, position
+        // (u % 8) ^ (row % 8)
+        auto st_chunk = [&](const uint32_t(&cv)[16], int ch) {
 #pragma unroll
-          for (int cc = 0; cc < 8; ++cc) {
+          for (int t = 0; t < 2; ++t) {
             uint32_t a[4];
 #pragma unroll
-            for (int t = 0; t < 4; ++t)
-              a[t] = pack2<BF16>(__uint_as_float(sv[cc * 8 + 2 * t]) * scale_out,
-                                 __uint_as_float(sv[cc * 8 + 2 * t + 1]) * scale_out);
-            st_shared_v4(prow + h2 * kHalf + ((cc ^ (row & 7)) << 4), a[0], a[1], a[2], a[3]);
+            for (int q = 0; q < 4; ++q)
+              a[q] = pack2<BF16>(__uint_as_float(cv[8 * t + 2 * q]) * scale_out,
+                                 __uint_as_float(cv[8 * t + 2 * q + 1]) * scale_out);
+            const int u = 2 * ch + t;
+            st_shared_v4(prow + (u >> 3) * kHalf + (((u & 7) ^ (row & 7)) << 4), a[0], a[1], a[2],
+                         a[3]);
           }
+        };
+        tmem_ld16(tS + 16 * c_lo, ca);
+        tmem_wait_ld();
+#pragma unroll 1
+        for (int ch = c_lo; ch < c_hi; ch += 2) {
+          tmem_ld16(tS + 16 * (ch + 1), cb);
+          st_chunk(ca, ch);
+          tmem_wait_ld();
+          if (ch + 2 < c_hi) tmem_ld16(tS + 16 * (ch + 2), ca);
+          st_chunk(cb, ch + 1);
+          tmem_wait_ld();
         }
         fence_proxy_async_smem();
       }
@@ -984,6 +1053,11 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   tp.hgroup = hgroup;
   const char* ea = getenv("MA_TC_EARLY");  // default on (measured faster with hgroup 2)
   tp.early = (ea && ea[0] == '0') ? 0 : 1;
+  tp.claim = 2;
+  const char* cl = getenv("MA_TC_CLAIM");
+  if (cl) tp.claim = atoi(cl);
+  if (tp.claim < 1) tp.claim = 1;
+  if (tp.claim > 16) tp.claim = 16;
   tp.sm_scale = s.sm_scale;
   tp.timeout_ns = 2000000000ull;  // 2 s per bounded wait
   const char* tmo = getenv("MA_WAIT_TIMEOUT_NS");

@@ -95,27 +95,36 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 // 128 fp32 accumulator columns of this lane -> scaled 16-bit into a 128-row
-// SW128 staging tile (row r of column half h at h*hstride + r*128, chunk c
-// at c ^ (r & 7))
+// SW128 staging tile (row r of column half h at h*hstride + r*128, 16-byte
+// unit c at c ^ (r & 7)); 16-column chunks, the next one's load in flight
 template <bool BF16>
 __device__ __forceinline__ void stage_row(uint32_t tile, uint32_t hstride, int row, uint32_t taddr,
                                           float scale) {
+  uint32_t ca[16], cb[16];
+  const uint32_t rbase = tile + row * 128;
+  auto put = [&](const uint32_t(&cv)[16], int ch) {
 #pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
-    uint32_t o[2][32];
-    tmem_ld32(taddr + h2 * 64, o[0]);
-    tmem_ld32(taddr + h2 * 64 + 32, o[1]);
-    tmem_wait_ld();
-    const uint32_t rbase = tile + h2 * hstride + row * 128;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
+    for (int t = 0; t < 2; ++t) {
       uint32_t w[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
-        w[t] = pack2<BF16>(__uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t]) * scale,
-                           __uint_as_float(o[c >> 2][(c & 3) * 8 + 2 * t + 1]) * scale);
-      st_shared_v4(rbase + ((c ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
+      for (int q = 0; q < 4; ++q)
+        w[q] = pack2<BF16>(__uint_as_float(cv[8 * t + 2 * q]) * scale,
+                           __uint_as_float(cv[8 * t + 2 * q + 1]) * scale);
+      const int u = 2 * ch + t;
+      st_shared_v4(rbase + (u >> 3) * hstride + (((u & 7) ^ (row & 7)) << 4), w[0], w[1], w[2],
+                   w[3]);
     }
+  };
+  tmem_ld16(taddr, ca);
+  tmem_wait_ld();
+#pragma unroll 1
+  for (int ch = 0; ch < 8; ch += 2) {
+    tmem_ld16(taddr + 16 * (ch + 1), cb);
+    put(ca, ch);
+    tmem_wait_ld();
+    if (ch + 2 < 8) tmem_ld16(taddr + 16 * (ch + 2), ca);
+    put(cb, ch + 1);
+    tmem_wait_ld();
   }
 }
 
@@ -450,35 +459,54 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
         u_b = -mx * kLog2e;
       }
       const bool colsub = KIND != K_R && KIND != K_RF;
+      // pass 2 in 16-column chunks (next chunk's TMEM load in flight), two
+      // columns per f32x2 instruction; P of chunk ch as packed 16-bit pairs
+      // into TMEM columns 8 ch .. 8 ch + 7 (S columns already read)
       float s4[4] = {0.f, 0.f, 0.f, 0.f}, w4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[64];
-        tmem_ld32(tS + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld32(tS + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        tmem_wait_ld();
-        const float4* cv = reinterpret_cast<const float4*>(vecA + 64 * c);
+      {
+        uint64_t s2[2] = {0ull, 0ull}, w2[2] = {0ull, 0ull};
+        const uint64_t ua2 = f2pack(u_a, u_a), ub2 = f2pack(u_b, u_b);
+        const uint64_t nl2 = f2pack(-kLog2e, -kLog2e);
+        uint32_t ca[16], cb[16];
+        auto exp_chunk = [&](uint32_t(&cv)[16], int ch) {
+          const uint64_t* vv = reinterpret_cast<const uint64_t*>(vecA + 16 * ch);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          float u = fmaf(__uint_as_float(sv[i]), u_a, u_b);
-          if (colsub) {
-            const float4 c4 = cv[i >> 2];
-            u -= kLog2e * ((i & 3) == 0 ? c4.x : (i & 3) == 1 ? c4.y : (i & 3) == 2 ? c4.z : c4.w);
+          for (int t = 0; t < 8; ++t) {
+            uint64_t u2 =
+                ffma2(f2pack(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1])), ua2, ub2);
+            if (colsub) u2 = ffma2(vv[t], nl2, u2);
+            float u0, u1;
+            f2unpack(u2, u0, u1);
+            const float e0 = ex2(u0), e1 = ex2(u1);
+            const uint64_t e2 = f2pack(e0, e1);
+            s2[t & 1] = fadd2(s2[t & 1], e2);
+            if (KIND == K_R || KIND == K_RF) w2[t & 1] = ffma2(e2, u2, w2[t & 1]);
+            cv[2 * t] = __float_as_uint(e0);
+            cv[2 * t + 1] = __float_as_uint(e1);
           }
-          const float ev = ex2(u);
-          s4[i & 3] += ev;
-          if (KIND == K_R || KIND == K_RF) w4[i & 3] = fmaf(ev, u, w4[i & 3]);
-          sv[i] = __float_as_uint(ev);
-        }
-        if (KIND != K_LS) {
-          // P as packed 16-bit pairs into TMEM columns 32c .. 32c+31: those
-          // S columns were read in this or an earlier chunk
-          uint32_t pk[32];
+          if (KIND != K_LS) {
+            uint32_t pk[8];
 #pragma unroll
-          for (int c2 = 0; c2 < 32; ++c2)
-            pk[c2] = pack2<BF16>(__uint_as_float(sv[2 * c2]), __uint_as_float(sv[2 * c2 + 1]));
-          tmem_st32(tS + 32 * c, pk);
+            for (int t = 0; t < 8; ++t)
+              pk[t] = pack2<BF16>(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1]));
+            tmem_st8(tS + 8 * ch, pk);
+          }
+        };
+        tmem_ld16(tS, ca);
+        tmem_wait_ld();
+#pragma unroll 1
+        for (int ch = 0; ch < 16; ch += 2) {
+          tmem_ld16(tS + 16 * (ch + 1), cb);
+          exp_chunk(ca, ch);
+          tmem_wait_ld();
+          if (ch + 2 < 16) tmem_ld16(tS + 16 * (ch + 2), ca);
+          exp_chunk(cb, ch + 1);
+          tmem_wait_ld();
         }
+        f2unpack(s2[0], s4[0], s4[1]);
+        f2unpack(s2[1], s4[2], s4[3]);
+        f2unpack(w2[0], w4[0], w4[1]);
+        f2unpack(w2[1], w4[2], w4[3]);
       }
       const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       if (KIND == K_R || KIND == K_RF) {
