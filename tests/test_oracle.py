@@ -60,6 +60,58 @@ def test_matrix_rows_sum_to_one():
     assert (A >= 0).all()
 
 
+def monarch_blocks(A: np.ndarray, B: int) -> np.ndarray:
+    """Dense (.., N, N) matrix -> (.., j, k, l, i) blocks with A[(l b + j), (k b + i)]."""
+    *lead, N, _ = A.shape
+    M = N // B
+    blk = A.reshape(*lead, M, B, M, B)            # l, j, k, i
+    return np.moveaxis(blk, (-4, -3, -2, -1), (-2, -4, -3, -1))  # j, k, l, i
+
+
+def objective(A: np.ndarray, q: np.ndarray, k: np.ndarray) -> np.ndarray:
+    """Variational objective <A, q k^T> / sqrt(d) - sum A log A per head,
+    as evaluated by vit/convergence.py:29-30 of the reference."""
+    d = q.shape[-1]
+    s = np.einsum("...nd,...md->...nm", q.astype(np.float64), k.astype(np.float64)) / np.sqrt(d)
+    a = A.astype(np.float64)
+    ent = np.where(a > 0, a * np.log(np.where(a > 0, a, 1.0)), 0.0)
+    return (a * s).sum((-2, -1)) - ent.sum((-2, -1))
+
+
+def test_matrix_is_monarch():
+    """With V = I the output is A = P L P^T R (ma/ma_history.py:10-12): entry
+    ((l, j), (k, i)) is L[j, k, l] * R[k, j, i], so for every (j, k) the
+    M x b block over (l, i) is an outer product (rank 1)."""
+    rng = np.random.default_rng(2)
+    E, H, N, D, B = 1, 2, 64, 16, 8
+    q = rng.standard_normal((E, H, N, D)).astype(np.float32) / 2
+    k = rng.standard_normal((E, H, N, D)).astype(np.float32) / 2
+    eye = np.broadcast_to(np.eye(N, dtype=np.float32), (E, H, N, N))
+    for T in (1, 2, 3):
+        A = monarch_attention_oracle(q, k, eye, None, T, B, False)
+        sv = np.linalg.svd(monarch_blocks(A, B).astype(np.float64), compute_uv=False)
+        assert (sv[..., 1] <= 1e-5 * sv[..., 0]).all(), T
+
+
+def test_objective_non_decreasing_in_steps():
+    """Each R-step and L-step maximises the objective over one factor with
+    the other fixed (coordinate ascent), so f(A_T) does not decrease with T."""
+    rng = np.random.default_rng(3)
+    E, H, N, D, B = 1, 3, 64, 16, 8
+    q = rng.standard_normal((E, H, N, D)).astype(np.float32)
+    k = rng.standard_normal((E, H, N, D)).astype(np.float32)
+    eye = np.broadcast_to(np.eye(N, dtype=np.float32), (E, H, N, N))
+    f = [objective(monarch_attention_oracle(q, k, eye, None, T, B, False), q, k) for T in range(1, 6)]
+    for a, b in zip(f, f[1:]):
+        assert (b >= a - 1e-4 * np.abs(a)).all(), (a, b)
+    assert (f[-1] > f[0]).all()
+    # softmax attention maximises f over all row-stochastic matrices
+    s = np.einsum("...nd,...md->...nm", q.astype(np.float64), k.astype(np.float64)) / np.sqrt(D)
+    sm = np.exp(s - s.max(-1, keepdims=True))
+    sm /= sm.sum(-1, keepdims=True)
+    assert (f[-1] <= objective(sm, q, k) + 1e-6).all()
+
+
 def test_fully_masked_sequence_has_no_nan():
     rng = np.random.default_rng(1)
     E, H, N, D, B = 2, 1, 40, 8, 8

@@ -284,6 +284,59 @@ def test_get_matrix_rows_sum_to_one(cuda_device):
     assert np.abs(A.cpu().numpy() - ref).max() <= F32_TOL
 
 
+def test_get_matrix_is_monarch_and_ascends(cuda_device):
+    """The CUDA path's matrix has the Monarch structure (every (j, k) block
+    over (l, i) is rank 1) and the variational objective does not decrease
+    with the number of steps (same properties as the oracle's tests)."""
+    from test_oracle import monarch_blocks, objective
+    g = torch.Generator(device="cpu").manual_seed(12)
+    E, H, N, D, B = 1, 4, 256, 64, 16
+    q, k = (torch.randn(E, H, N, D, generator=g).to(cuda_device) / 2 for _ in range(2))
+    qn, kn = q.cpu().numpy(), k.cpu().numpy()
+    fs = []
+    for T in (1, 2, 3, 4):
+        A = MonarchAttention(B, T, PadType.post).get_matrix(q, k).cpu().numpy()
+        sv = np.linalg.svd(monarch_blocks(A, B).astype(np.float64), compute_uv=False)
+        assert (sv[..., 1] <= 1e-4 * sv[..., 0]).all(), T
+        fs.append(objective(A, qn, kn))
+    for a, b in zip(fs, fs[1:]):
+        assert (b >= a - 1e-4 * np.abs(a)).all(), (a, b)
+
+
+@pytest.mark.parametrize("name", ["long4k_bf16", "long16k_bf16", "long64k_bf16"])
+def test_full_size_properties(name, cuda_device):
+    """Size-independent checks over every head of the full-size tensor-core
+    workloads: the output is linear in V (A depends on q and k only), and
+    heads are independent (permuting the (e, h) heads permutes the output
+    bit for bit, whatever wavefront order and workspace slots they get)."""
+    cfg = CONFIGS[name]
+    q, k, v, mask, _ = make_inputs(cfg, device=cuda_device)
+
+    def f(q_, k_, v_):
+        return monarch_attention(q_, k_, v_, mask, cfg.T, cfg.B, cfg.pre_pad)
+
+    g = torch.Generator(device=cuda_device).manual_seed(11)
+    v2 = torch.randn(v.shape, generator=g, device=cuda_device).to(v.dtype)
+    o1 = f(q, k, v)
+    o2 = f(q, k, v2)
+    o3 = f(q, k, (v.float() + v2.float()).to(v.dtype))
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    scale = o3.float().abs().max().item()
+    err = (o3.float() - o1.float() - o2.float()).abs().max().item()
+    assert err <= LP_TOL * scale, f"linearity: max|err|={err:.3g} (max|out|={scale:.3g})"
+    E, H = q.shape[:2]
+    perm = torch.randperm(E * H, generator=torch.Generator().manual_seed(5)).to(cuda_device)
+
+    def shuf(t):
+        return t.reshape(E * H, *t.shape[2:])[perm].reshape(t.shape)
+
+    o4 = f(shuf(q), shuf(k), shuf(v))
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert torch.equal(o4, shuf(o1))
+
+
 def test_module_forward_matches_function(cuda_device):
     cfg = CONFIGS["vit_bf16"].with_(E=1, H=2)
     q, k, v, _, _ = make_inputs(cfg, device=cuda_device)
