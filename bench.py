@@ -383,10 +383,16 @@ def run_gpu(args, cfg, rank, world, local_rank):
                "ms_per_step": e2e_ms, "steps": n_e2e, "pipelined": "double-buffered copy streams",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": hout[0].numel() * hout[0].element_size()}
 
+    verify = None
     if args.verify and world > 1:
+        # every rank's output shard over NCCL to every rank (after timing);
+        # rank 0 checks the shards are finite and that its own came back intact
         gathered = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(gathered, out)
         torch.cuda.synchronize()
+        verify = {"gathered_bytes": sum(t.numel() * t.element_size() for t in gathered),
+                  "all_finite": bool(all(torch.isfinite(t).all().item() for t in gathered)),
+                  "own_shard_equal": bool(torch.equal(gathered[rank], out))}
 
     # ---- roofline of the dominant kernel (one forward = one launch on tc)
     peaks, peak_src = load_peaks()
@@ -436,6 +442,8 @@ def run_gpu(args, cfg, rank, world, local_rank):
             "gpu_launches": launches_per_fwd * args.steps, "clocks": clk,
             "device_status": status,
         }
+        if verify is not None:
+            line["verify"] = verify
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
