@@ -34,6 +34,10 @@ struct Shape {
 //   y  [b][M][Dv] (storage dtype)   -- final R-step output
 //   ar [M][b][D]  (storage dtype)   -- L-step output, R-step input
 //   cl [b][M] fp32, cr [M][b] fp32  -- row/column statistics
+//   clx [b][M] x 16 bytes           -- cl as a 16-bit (hi, lo) pair padded to
+//                                      16 bytes (tcgen05 kernel, b = 64 / 128:
+//                                      the operand of the GEMM step that
+//                                      subtracts cl; 0 = not used)
 //   lmax, lsum [b][M] fp32          -- L-step softmax statistics (generic path)
 //   ctrl                            -- dependency counters (tcgen05 path)
 //   xq, xk, xv                      -- bf16 copies of e4m3 q / k / v for the
@@ -43,7 +47,7 @@ struct Shape {
 //                                      slot limit; every head in ma_fwd's
 //                                      workspace, fewer in compact ones)
 struct WsLayout {
-  size_t al, y, ar, cl, cr, lmax, lsum, ctrl, ctrl_bytes, total;
+  size_t al, y, ar, cl, cr, clx, lmax, lsum, ctrl, ctrl_bytes, total;
   size_t xq, xk, xv;
   int tc_slots;
   int store_bytes;  // bytes per element of al / y / ar

@@ -94,6 +94,7 @@ ma::WsLayout compact_layout(const ma::Shape& s, int slots, size_t* status_off) {
   w.ar = off; off = ma::align_up(off + slots * bm * s.D * 2, 256);
   w.cl = off; off = ma::align_up(off + slots * bm * 4, 256);
   w.cr = off; off = ma::align_up(off + slots * bm * 4, 256);
+  w.clx = off; off = ma::align_up(off + slots * bm * 16, 256);
   w.tc_slots = slots;
   w.lmax = w.lsum = off;  // unused by the tcgen05 kernel
   *status_off = off; off = ma::align_up(off + 4, 256);

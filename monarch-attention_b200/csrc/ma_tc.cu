@@ -72,10 +72,20 @@ constexpr int kOffDesc = 256;     // item descriptors of the ring entries (kEntr
 constexpr int kOffEnd = 320;      // number of items this CTA was given (set at the end)
 constexpr int kOffTmem = 324;     // TMEM base address
 constexpr int kOffItems = 384;    // item descriptors by item index (kItemRing x int4)
-constexpr int kOffVec = 512;      // per entry: cr[m][:] or cl[j][:] (kEntries x 512 B)
-constexpr int kOffOnes = 2048;    // ones operand of the cr GEMM (512 B)
-constexpr int kOffScale = 2560;   // output scale per row (kScaleRing x 128 fp32)
-constexpr int kSmallBytes = kOffScale + kScaleRing * 512;
+constexpr int kOffOnes = 512;     // ones operand of the cr GEMM (512 B)
+constexpr int kOffScale = 1024;   // output scale per row (kScaleRing x 128 fp32)
+// The cl subtraction of L / output items runs on the tensor core as a ninth
+// K step of GEMM1: A_ext (128 rows x 16 columns: -1, -1, 0 ...) times B_ext
+// (row k: cl_hi[k], cl_lo[k], 0 ..., cl split into two 16-bit values) adds
+// -(cl_hi + cl_lo) = -cl[k] to column k of S.  Both are K-major tiles
+// without swizzle: 8-row core matrices of 16 bytes per row, row groups 128 B
+// apart (SBO), the K = 8..15 half read from a zero block (LBO).
+constexpr int kOffExtA = 3072;    // A_ext (2 KB)
+constexpr int kOffVec = 5120;     // per entry: B_ext rows of cl[j][:] (L / out, 2 KB)
+                                  // or the cr[m][:] vector (R, 512 B fp32)
+constexpr int kExtBytes = 2048;
+constexpr int kOffZero = kOffVec + kEntries * kExtBytes;  // 2 KB of zeros
+constexpr int kSmallBytes = kOffZero + kExtBytes;
 constexpr int kTileRegion = kEntries * kEntryBytes;
 constexpr int kSmemBytes = kSmallBytes + 1024 + kTileRegion;  // + worst-case alignment pad
 static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -120,7 +130,7 @@ struct TcParams {
   char* al;
   char* ar;
   char* y;
-  float* cl;
+  uint4* clx;   // cl[j][k] as B_ext rows: (hi, lo) 16-bit pair padded to 16 bytes
   float* cr;
   uint32_t* ctrl;
   uint32_t* status;
@@ -271,6 +281,11 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
     const uint32_t one = BF16 ? 0x3F803F80u : 0x3C003C00u;
     st_shared_v4(sbase + kOffOnes + tid * 16, one, one, one, one);
   }
+  if (tid < 128) {  // A_ext row (-1, -1, 0, ...) and the zero block
+    const uint32_t m1 = BF16 ? 0xBF80BF80u : 0xBC00BC00u;
+    st_shared_v4(sbase + kOffExtA + tid * 16, m1, 0u, 0u, 0u);
+    st_shared_v4(sbase + kOffZero + tid * 16, 0u, 0u, 0u, 0u);
+  }
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -362,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const int slot = head % p.slots;
         const int eb = head / p.H, hh = head - eb * p.H;
         const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
-        const uint32_t vdst = sbase + kOffVec + e * 512;
+        const uint32_t vdst = sbase + kOffVec + e * kExtBytes;
         // first row of the tile in the per-slot arrays ar [M][b], al / y
         // [b][M], cr [M][b], cl [b][M] (rows of D / Dv elements or floats),
         // and its first token in q / k / v
@@ -387,8 +402,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
                           final_ ? once : keep);
           }
         } else {
-          mbar_expect_tx(fb, 2 * kTileBytes + 512);
-          bulk_load(vdst, p.cl + vrow, 512, fb);
+          mbar_expect_tx(fb, 2 * kTileBytes + kExtBytes);
+          bulk_load(vdst, p.clx + vrow, kExtBytes, fb);
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
             // Q_j: tokens j, j + b, j + 2b, ... of each index j of the tile
@@ -423,6 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
     if (lane == 0) {
       constexpr uint32_t id_mm = idesc_f16(BF16, true, true, 128, 128);  // ar = P^T Q_j
       constexpr uint32_t id_cr = idesc_f16(BF16, true, false, 128, 16);  // cr = P^T 1
+      constexpr uint32_t id_ext = idesc_f16(BF16, false, false, 128, 128);  // S -= cl
       const uint32_t ones = sbase + kOffOnes;
       uint32_t m = 0;                     // next item for GEMM1
       uint32_t n = 0;                     // next item for GEMM2
@@ -493,10 +509,17 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
                 }
               }
               if (ok) {
-                prev_kind[gm] = desc_slot[e].w;
+                const int kind1 = desc_slot[e].w;
+                prev_kind[gm] = kind1;
                 tc_fence_after();
                 const uint32_t A = tbase + e * kEntryBytes;
                 gemm1<BF16>(tmem + 256 * gm, A, A + kTileBytes);
+                if (kind1 != KIND_R) {  // S - cl[k] (L / output items): the ninth K step
+                  const uint32_t xa = sbase + kOffExtA, xb = sbase + kOffVec + e * kExtBytes;
+                  const uint32_t z = sbase + kOffZero;
+                  mma_ss(tmem + 256 * gm, smem_desc(xa, z - xa, 128, kSwzNone),
+                         smem_desc(xb, z - xb, 128, kSwzNone), id_ext, 1);
+                }
                 mma_commit(bar(kBarSFull, gm));
                 trace_stamp(p, m, 3, globaltimer());
                 ++m;
@@ -563,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       const bool final_ = kind == KIND_R && ph == P - 2;
       const int eb = head / p.H, hh = head - eb * p.H;
       const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
-      const float* vec = vec0 + e * 128;  // cr[m][:] (R) or cl[j][:] (L / out)
+      const float* vec = vec0 + e * (kExtBytes / 4);  // cr[m][:] (R items)
       const int trow = slot * BLK * BLK + item * kT;  // tile's first row in the slot arrays
       // the item of this row within the tile and, for BLK = 64, the 64-column
       // half of S / P that belongs to it (warp-uniform: 64 rows = 2 warps)
@@ -591,8 +614,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const char* tile = (kind == KIND_R ? p.ar : p.al) + (size_t)trow * kT * 2;
         discard_l2(tile + row * 128);
         discard_l2(tile + (row + 128) * 128);
-        if (row < 4)
-          discard_l2(reinterpret_cast<const char*>((kind == KIND_R ? p.cr : p.cl) + trow) + row * 128);
+        if (kind == KIND_R ? row < 4 : row < kExtBytes / 128)  // the cr vector or the cl rows
+          discard_l2((kind == KIND_R ? reinterpret_cast<const char*>(p.cr + trow)
+                                     : reinterpret_cast<const char*>(p.clx + trow)) +
+                     row * 128);
       }
 
       // The row of S (128 fp32) is streamed out of TMEM in 16-column chunks,
@@ -610,24 +635,18 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       float mx;
       {
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        auto max_chunk = [&](const uint32_t(&cv)[16], int ch) {
-          if (rk) {
+        // (L / output items: S already holds x = S - cl[k], from GEMM1)
+        auto max_chunk = [&](const uint32_t(&cv)[16]) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(cv[i]));
-          } else {
-            const float* vv = vec + 16 * ch;
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(cv[i]) - vv[i]);
-          }
+          for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(cv[i]));
         };
 #pragma unroll 1
         for (int ch = c_lo; ch < c_hi; ch += 2) {  // the maximum needs no prefetch
           tmem_ld16(tS + 16 * ch, ca);
           tmem_ld16(tS + 16 * (ch + 1), cb);
           tmem_wait_ld();
-          max_chunk(ca, ch);
-          max_chunk(cb, ch + 1);
+          max_chunk(ca);
+          max_chunk(cb);
         }
         mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
@@ -639,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         u_a = c * kLog2e;
         u_b = -mxt * kLog2e;
       } else {
-        u_a = kLog2e;  // x = S - cl[k]
+        u_a = kLog2e;  // x = S - cl[k] (subtracted by GEMM1)
         u_b = -mx * kLog2e;
       }
       float s4[4] = {0.f, 0.f, 0.f, 0.f}, w4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -650,11 +669,9 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         // 16-bit pairs into columns 8 ch .. 8 ch + 7 (R / out: those S
         // columns were read already, and the chunk in flight lies beyond)
         auto exp_chunk = [&](uint32_t(&cv)[16], int ch) {
-          const uint64_t* vv = reinterpret_cast<const uint64_t*>(vec + 16 * ch);
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
-            uint64_t x2 = f2pack(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1]));
-            if (!rk) x2 = fsub2(x2, vv[t]);
+            const uint64_t x2 = f2pack(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1]));
             const uint64_t u2 = ffma2(x2, ua2, ub2);
             float u0, u1;
             f2unpack(u2, u0, u1);
@@ -705,9 +722,14 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const float den = sum + kEps;  // r = e / (sum + eps), :17
         const float inv = 1.0f / den;
         // cl = sum_i r_i log r_i, log r_i = (t_i - mx) - log(den)  (:20)
-        // cl[j][m] of this row: j = row % BLK, m = the row's key block
-        p.cl[(size_t)(slot * BLK + row % BLK) * BLK + item * PACK + pk_row] =
-            kLn2 * inv * wsum - __logf(den) * sum * inv;
+        // cl[j][m] of this row: j = row % BLK, m = the row's key block; stored
+        // as the B_ext row of the later GEMM that subtracts it: cl split into
+        // a 16-bit value and the 16-bit rounding of the remainder (their sum
+        // carries ~16 significant bits)
+        const float clv = kLn2 * inv * wsum - __logf(den) * sum * inv;
+        const float hi = round16<BF16>(clv);
+        p.clx[(size_t)(slot * BLK + row % BLK) * BLK + item * PACK + pk_row] =
+            make_uint4(pack2<BF16>(hi, clv - hi), 0u, 0u, 0u);
         scale_out = inv;
       } else {
         scale_out = 1.0f / sum;
@@ -1041,7 +1063,8 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   tp.al = w + ws.al;
   tp.ar = w + ws.ar;
   tp.y = w + ws.y;
-  tp.cl = reinterpret_cast<float*>(w + ws.cl);
+  tp.clx = reinterpret_cast<uint4*>(w + ws.clx);
+  if (ws.clx == 0) return cudaErrorInvalidValue;  // the layout has no cl rows for this shape
   tp.cr = reinterpret_cast<float*>(w + ws.cr);
   tp.ctrl = reinterpret_cast<uint32_t*>(w + ws.ctrl);
   tp.status = p->status;

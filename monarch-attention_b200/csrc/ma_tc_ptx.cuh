@@ -254,6 +254,13 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// the value of x rounded to the 16-bit storage type (bf16 or fp16)
+template <bool BF16>
+__device__ __forceinline__ float round16(float x) {
+  if (BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  return __half2float(__float2half_rn(x));
+}
+
 // packed fp32 pairs (sm_100a f32x2 arithmetic): two lanes per instruction
 __device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
   uint64_t r;
