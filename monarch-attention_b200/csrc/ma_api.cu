@@ -84,8 +84,11 @@ WsLayout make_layout(const Shape& s, int dtype, bool conv) {
   w.ar = off; off = align_up(off + heads * bm * s.D * w.store_bytes, 256);
   w.cl = off; off = align_up(off + heads * bm * 4, 256);
   w.cr = off; off = align_up(off + heads * bm * 4, 256);
-  if (s.D == 128 && s.b == s.M && (s.b == 64 || s.b == 128)) {  // tcgen05 kernel shapes
+  if (s.D == 128 && s.b == s.M && (s.b == 64 || s.b == 128 || s.b == 256)) {  // tcgen05 shapes
     w.clx = off; off = align_up(off + heads * bm * 16, 256);
+    if (s.b == 256) {
+      w.lsex = off; off = align_up(off + heads * bm * 16, 256);
+    }
   }
   w.lmax = off; off = align_up(off + heads * bm * 4, 256);
   w.lsum = off; off = align_up(off + heads * bm * 4, 256);

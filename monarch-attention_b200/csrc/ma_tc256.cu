@@ -50,9 +50,17 @@ constexpr uint32_t kTmemCols = 256;
 // small region: barriers, TMEM address, vectors
 constexpr int kOffBar = 0;
 constexpr int kOffTmem = 128;
-constexpr int kOffVecA = 256;                 // per-column vector (cl[k] or lse[l]): 256 fp32
-constexpr int kOffVecB = kOffVecA + 1024;     // per-row vector (cr[j] or cl[k]): 128 fp32
-constexpr int kSmallBytes = kOffVecB + 512;
+constexpr int kOffVecB = 256;                 // per-row vector (cr[j] or cl[k]): 128 fp32
+// The per-column term of LS / LA / output tiles (cl[k] or lse[l]) is
+// subtracted on the tensor core by a ninth K step of GEMM1: A_ext (128 rows:
+// -1, -1, 0 ...) times B_ext (256 rows: the term split into a 16-bit value
+// and the 16-bit rounding of its remainder, 0 ...), K-major without
+// swizzle (8-row core matrices of 16-byte rows 128 B apart; the K = 8..15
+// half read from a zero block).
+constexpr int kOffExtA = 1024;                // A_ext: 128 x 16 B
+constexpr int kOffExtB = kOffExtA + 2048;     // B_ext: 256 x 16 B (clx / lsex rows)
+constexpr int kOffZero = kOffExtB + 4096;     // 4 KB of zeros
+constexpr int kSmallBytes = kOffZero + 4096;
 constexpr int kSmemBytes = kSmallBytes + 1024 + kABytes + kBBytes;  // + alignment pad
 
 // barriers (8 B each)
@@ -80,8 +88,9 @@ struct Params {
   CUtensorMap tm_ar_st;  // ar as (D, b, heads*M): rows k of index j
   CUtensorMap tm_out_st; // out as (Dv, b, M, H, E): tokens l*b + j
   float* cl;             // [head][j][m]
+  uint4* clx;            // cl as B_ext rows: (hi, lo) 16-bit pair padded to 16 bytes
   float* cr;             // [head][m][j]
-  float* lse;            // [head][j][l]: log-sum-exp of the L-step rows
+  uint4* lsex;           // [head][j][l]: log-sum-exp of the L-step rows, as B_ext rows
   uint32_t* abort;
   uint32_t* status;
   int H;
@@ -137,7 +146,6 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const Guard guard{p.abort, p.status, p.timeout_ns};
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem_raw + kOffTmem);
-  const float* vecA = reinterpret_cast<const float*>(smem_raw + kOffVecA);
   const float* vecB = reinterpret_cast<const float*>(smem_raw + kOffVecB);
   auto bar = [&](int off) { return sbase + kOffBar + off; };
   constexpr bool has_o = KIND != K_LS;
@@ -171,6 +179,12 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
     mbar_init(bar(kBarX2), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  for (int i = tid; i < 256; i += kThreads) {  // A_ext rows (-1, -1, 0 ...) and the zero block
+    const uint32_t m1 = BF16 ? 0xBF80BF80u : 0xBC00BC00u;
+    if (i < kRows) st_shared_v4(sbase + kOffExtA + i * 16, m1, 0u, 0u, 0u);
+    st_shared_v4(sbase + kOffZero + i * 16, 0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_smem();
   if (warp == kIssueWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_holder)),
@@ -192,19 +206,19 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
     if (lane == 0) {
       const uint64_t keep = policy_evict_last(), once = policy_evict_first();
       const uint32_t fb = bar(kBarFull);
-      const uint32_t va = sbase + kOffVecA, vb = sbase + kOffVecB;
+      const uint32_t va = sbase + kOffExtB, vb = sbase + kOffVecB;
       uint32_t vbytes = 0;
       if (KIND == K_R || KIND == K_RF) vbytes = p.first ? 0 : 512;  // cr[m][j-tile]
-      if (KIND == K_LS || KIND == K_O) vbytes = 1024;               // cl[j][:]
-      if (KIND == K_LA) vbytes = 1024 + 512;                        // lse[j][:], cl[j][k-tile]
+      if (KIND == K_LS || KIND == K_O) vbytes = 4096;               // cl[j][:] rows
+      if (KIND == K_LA) vbytes = 4096 + 512;                        // lse[j][:] rows, cl[j][k-tile]
       auto load_vec = [&](const TileId& d) {
         if (KIND == K_R || KIND == K_RF) {
           if (!p.first)
             bulk_load(vb, p.cr + (size_t)(d.hrow + d.item) * kCols + d.rt * kRows, 512, fb);
         } else if (KIND == K_LS || KIND == K_O) {
-          bulk_load(va, p.cl + (size_t)(d.hrow + d.item) * kCols, 1024, fb);
+          bulk_load(va, p.clx + (size_t)(d.hrow + d.item) * kCols, 4096, fb);
         } else {
-          bulk_load(va, p.lse + (size_t)(d.hrow + d.item) * kCols, 1024, fb);
+          bulk_load(va, p.lsex + (size_t)(d.hrow + d.item) * kCols, 4096, fb);
           bulk_load(vb, p.cl + (size_t)(d.hrow + d.item) * kCols + d.rt * kRows, 512, fb);
         }
       };
@@ -275,6 +289,11 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
           const uint32_t offb = (kk >> 2) * kBHalf + (kk & 3) * 32;
           mma_ss(tmem, smem_desc(A + offa, 16, 1024, kSwz128),
                  smem_desc(B + offb, 16, 1024, kSwz128), id1, kk > 0);
+        }
+        if (KIND == K_LS || KIND == K_LA || KIND == K_O) {  // S - column term: ninth K step
+          const uint32_t xa = sbase + kOffExtA, xb = sbase + kOffExtB, z = sbase + kOffZero;
+          mma_ss(tmem, smem_desc(xa, z - xa, 128, kSwzNone), smem_desc(xb, z - xb, 128, kSwzNone),
+                 id1, 1);
         }
         mma_commit(bar(kBarS));
         if (KIND == K_LS) {
@@ -430,25 +449,14 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
           tmem_ld32(tS + 64 * c, *reinterpret_cast<uint32_t(*)[32]>(sv));
           tmem_ld32(tS + 64 * c + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
           tmem_wait_ld();
-          if (KIND == K_R || KIND == K_RF) {
+          // (LS / output tiles: S already holds x = S - cl[k], from GEMM1)
 #pragma unroll
-            for (int i = 0; i < 64; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[i]));
-          } else {
-            const float4* cv = reinterpret_cast<const float4*>(vecA + 64 * c);
-#pragma unroll
-            for (int i4 = 0; i4 < 16; ++i4) {
-              const float4 c4 = cv[i4];
-              mx4[0] = fmaxf(mx4[0], __uint_as_float(sv[4 * i4]) - c4.x);
-              mx4[1] = fmaxf(mx4[1], __uint_as_float(sv[4 * i4 + 1]) - c4.y);
-              mx4[2] = fmaxf(mx4[2], __uint_as_float(sv[4 * i4 + 2]) - c4.z);
-              mx4[3] = fmaxf(mx4[3], __uint_as_float(sv[4 * i4 + 3]) - c4.w);
-            }
-          }
+          for (int i = 0; i < 64; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(sv[i]));
         }
         mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       }
-      // exponent in log2 units: u = u_a * S + u_b - col_k * log2e (columns
-      // subtract cl[k] for LS / O, lse[l] for LA)
+      // exponent in log2 units: u = u_a * S + u_b (for LS / O, S - cl[k];
+      // for LA, S - lse[l]: GEMM1 subtracted the column term)
       float u_b;
       if (KIND == K_R || KIND == K_RF) {
         const float mxt = fmaxf(u_a * kLn2 * mx, kEps);  // clamp(max, eps) of t (:14-16)
@@ -458,7 +466,6 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
       } else {
         u_b = -mx * kLog2e;
       }
-      const bool colsub = KIND != K_R && KIND != K_RF;
       // pass 2 in 16-column chunks (next chunk's TMEM load in flight), two
       // columns per f32x2 instruction; P of chunk ch as packed 16-bit pairs
       // into TMEM columns 8 ch .. 8 ch + 7 (S columns already read)
@@ -466,15 +473,12 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
       {
         uint64_t s2[2] = {0ull, 0ull}, w2[2] = {0ull, 0ull};
         const uint64_t ua2 = f2pack(u_a, u_a), ub2 = f2pack(u_b, u_b);
-        const uint64_t nl2 = f2pack(-kLog2e, -kLog2e);
         uint32_t ca[16], cb[16];
         auto exp_chunk = [&](uint32_t(&cv)[16], int ch) {
-          const uint64_t* vv = reinterpret_cast<const uint64_t*>(vecA + 16 * ch);
 #pragma unroll
           for (int t = 0; t < 8; ++t) {
-            uint64_t u2 =
+            const uint64_t u2 =
                 ffma2(f2pack(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1])), ua2, ub2);
-            if (colsub) u2 = ffma2(vv[t], nl2, u2);
             float u0, u1;
             f2unpack(u2, u0, u1);
             const float e0 = ex2(u0), e1 = ex2(u1);
@@ -513,13 +517,22 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
         const float wsum = (w4[0] + w4[1]) + (w4[2] + w4[3]);
         const float den = sum + kEps;  // r = e / (sum + eps), :17
         const float inv = 1.0f / den;
-        // cl[j][m] = sum_i r_i log r_i (:20); this row is j = 128*rt + row
-        p.cl[(size_t)(d.hrow + d.rt * kRows + row) * kCols + d.item] =
-            kLn2 * inv * wsum - __logf(den) * sum * inv;
+        // cl[j][m] = sum_i r_i log r_i (:20); this row is j = 128*rt + row;
+        // fp32 for the LA tiles' rows, and as the B_ext row of the GEMM1 step
+        // of LS / output tiles (16-bit value + 16-bit remainder)
+        const float clv = kLn2 * inv * wsum - __logf(den) * sum * inv;
+        const size_t ci = (size_t)(d.hrow + d.rt * kRows + row) * kCols + d.item;
+        p.cl[ci] = clv;
+        const float hi = round16<BF16>(clv);
+        p.clx[ci] = make_uint4(pack2<BF16>(hi, clv - hi), 0u, 0u, 0u);
         scale_out = inv;
       } else if (KIND == K_LS) {
-        // lse[j][l] = max_k x + log(sum_k exp(x - max))
-        p.lse[(size_t)(d.hrow + d.item) * kCols + d.rt * kRows + row] = mx + __logf(sum);
+        // lse[j][l] = max_k x + log(sum_k exp(x - max)), as the B_ext row of
+        // the GEMM1 step of LA tiles
+        const float lse = mx + __logf(sum);
+        const float hi = round16<BF16>(lse);
+        p.lsex[(size_t)(d.hrow + d.item) * kCols + d.rt * kRows + row] =
+            make_uint4(pack2<BF16>(hi, lse - hi), 0u, 0u, 0u);
       } else if (KIND == K_LA) {
         // cr[k][j] = sum_l L[k][l] (:32); this row is k = 128*rt + row
         p.cr[(size_t)(d.hrow + d.rt * kRows + row) * kCols + d.item] = sum;
@@ -698,7 +711,9 @@ cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
   if (!ok) return cudaErrorInvalidValue;
   prm.cl = reinterpret_cast<float*>(w + ws.cl);
   prm.cr = reinterpret_cast<float*>(w + ws.cr);
-  prm.lse = reinterpret_cast<float*>(w + ws.lmax);
+  prm.clx = reinterpret_cast<uint4*>(w + ws.clx);
+  prm.lsex = reinterpret_cast<uint4*>(w + ws.lsex);
+  if (ws.clx == 0 || ws.lsex == 0) return cudaErrorInvalidValue;  // layout without the rows
   prm.abort = reinterpret_cast<uint32_t*>(w + ws.ctrl) + 1;
   prm.status = p->status;
   prm.H = s.H;
