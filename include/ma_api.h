@@ -130,8 +130,9 @@ size_t ma_workspace_bytes(const ma_fwd_params* p);
 int ma_fwd(const ma_fwd_params* p, void* stream);
 
 /* Same forward as ma_fwd(), for callers that cannot allocate device memory
- * (e.g. inside a stream capture that must not allocate, or a runtime whose
- * memory pool forbids foreign allocations): the scratch comes from a 64 MiB
+ * (e.g. a runtime whose memory pool forbids foreign allocations, or a
+ * serving loop with a fixed device-memory budget where an allocation could
+ * block or fail): the scratch comes from a 64 MiB
  * array compiled into the library instead of p->workspace, which is ignored.
  * No counterpart in the reference (its PyTorch implementation allocates its
  * intermediates per call, ma/ma_torch.py:89).

@@ -2,10 +2,10 @@
 // scratch array that lives in the library itself.
 //
 // Who needs it: callers that cannot call cudaMalloc (or any allocator) on the
-// path that runs the attention -- e.g. code running inside a CUDA stream
-// capture that must not allocate, an embedding runtime whose memory pool is
-// owned elsewhere and forbids foreign allocations, or a real-time loop where
-// an allocation could block.  They pass q / k / v / out and nothing else; the
+// path that runs the attention -- e.g. an embedding runtime whose memory pool
+// is owned elsewhere and forbids foreign allocations, or a real-time serving
+// loop with a fixed device-memory budget where an allocation could block or
+// fail.  They pass q / k / v / out and nothing else; the
 // kernel's scratch (the workspace slots of its intermediates and its control
 // counters) comes from g_ma_noalloc_scratch below.
 //

@@ -1,8 +1,8 @@
 """The allocation-free entry point ma_fwd_noalloc against ma_fwd.
 
 ma_fwd_noalloc exists for callers that cannot allocate device memory on the
-path that runs the attention (a stream capture that must not allocate, a
-runtime that owns the memory pool): it takes only q / k / v / out and runs
+path that runs the attention (a runtime that owns the memory pool, a serving
+loop with a fixed device-memory budget): it takes only q / k / v / out and runs
 the tcgen05 kernel on a scratch array compiled into the library.  This file
 calls it through the C ABI, twice in a row on different inputs, and checks
 each result against the regular entry point on the same inputs, within the
