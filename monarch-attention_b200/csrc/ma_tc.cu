@@ -23,10 +23,11 @@
 //
 // CTA roles (512 threads, one CTA per SM):
 //   warpgroups 0, 1  softmax; group g takes the items n with n % 2 == g
-//                    (ping-pong), thread i owns row i = TMEM lane i
+//                    (ping-pong), thread i owns row i = TMEM lane i; the
+//                    group's thread 0 issues the item's GEMM2 once P is ready
 //   warpgroup 2      epilogue (O -> 16-bit staging in shared memory)
 //   warp 12          scheduler + TMA producer (3-entry ring, 2 tiles each)
-//   warp 13          TMEM allocator + tcgen05.mma issuer
+//   warp 13          TMEM allocator + GEMM1 issuer
 //   warps 14, 15     TMA stores + publication of alternate items
 // The softmax and the epilogue stream each row out of TMEM in 16-column
 // chunks, the next chunk's load in flight while the current one is
@@ -101,6 +102,8 @@ constexpr int kBarOFree = 120;   // [2] O of the group read (128 arrivals per pa
 constexpr int kBarCrTaken = 136; // [2] cr read out of S (L items, 128 arrivals)
 constexpr int kBarDrain = 160;   // MMA drain before the end
 constexpr int kBarStaged = 168;  // [kEntries] output tile(s) of the entry's item staged (128)
+constexpr int kBarG2 = 192;      // [2] GEMM2 (all parts) of the group's item issued
+constexpr int kBarDrain2 = 208;  // [2] MMAs a softmax group issued, complete (at the end)
 
 // TMEM columns (fp32, 128 lanes): per group g, S/P at 256 g and O at 256 g + 128
 constexpr uint32_t kTmemCols = 512;
@@ -267,6 +270,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
     }
     for (int i = 0; i < kEntries; ++i) mbar_init(bar(kBarStaged, i), 128);
     mbar_init(bar(kBarDrain, 0), 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(kBarG2, g), 1);
+      mbar_init(bar(kBarDrain2, g), 1);
+    }
     *n_end_s = 0xFFFFFFFFu;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -429,139 +436,60 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       }
     }
   } else if (warp == kMmaWarp) {
-    // ===================== tcgen05.mma issuer =====================
-    // Non-blocking event loop: any item's loads may wait on earlier items of
-    // this CTA (dependencies are per phase), so the issuer never blocks on
-    // one condition while other issuable work exists.  GEMM1 of item m runs
-    // ahead (m <= n + 1: S of the group is free once GEMM2 of item m-2 was
-    // issued -- the tensor pipe executes MMAs in issue order).
+    // ===================== GEMM1 issuer =====================
+    // GEMM1 (and the cl step) of every item in order; GEMM2 is issued by the
+    // item's softmax group once its P is ready.  GEMM1 of item m reuses S of
+    // its group, so it waits until GEMM2 of item m - 2 (same group) has been
+    // issued (kBarG2; the tcgen05 fences around that barrier order the two).
     if (lane == 0) {
-      constexpr uint32_t id_mm = idesc_f16(BF16, true, true, 128, 128);  // ar = P^T Q_j
-      constexpr uint32_t id_cr = idesc_f16(BF16, true, false, 128, 16);  // cr = P^T 1
       constexpr uint32_t id_ext = idesc_f16(BF16, false, false, 128, 128);  // S -= cl
-      const uint32_t ones = sbase + kOffOnes;
-      uint32_t m = 0;                     // next item for GEMM1
-      uint32_t n = 0;                     // next item for GEMM2
-      int part = 0;                       // GEMM2 parts of item n already issued
-      bool x_ok = false;                  // late X tile of item n observed
-      uint32_t n_end = 0xFFFFFFFFu;       // known once the end marker is seen
-      uint32_t parts[2] = {0, 0};         // O parts committed per group
       uint32_t cr_waits[2] = {0, 0};      // cr_taken phases consumed per group
       int prev_kind[2] = {-1, -1};        // kind of the group's previous item
-      uint32_t xcnt[kEntries] = {0, 0, 0};  // late-X phases consumed per entry
-      uint64_t t_last = globaltimer();
-      for (uint32_t spin = 0;; ++spin) {
-        bool progressed = false;
-        // ---- GEMM2 (one part) of item n ----
-        if (n < m) {
-          const int e = n % kEntries, g = n & 1;
-          const int4 d = desc_slot[e];
-          const bool two = d.w == KIND_R && d.y == P - 2;  // R-final: al part, then y part
-          const bool needx = d.w == KIND_O || (two && part == 1);
-          bool ready = part > 0 || mbar_test(bar(kBarPReady, g), (n >> 1) & 1);
-          if (ready && needx && !x_ok) {
-            ready = mbar_test(bar(kBarX, e), xcnt[e] & 1);
-            if (ready) {
-              x_ok = true;
-              ++xcnt[e];
-            }
-          }
-          if (ready && parts[g] > 0) ready = mbar_test(bar(kBarOFree, g), (parts[g] - 1) & 1);
-          if (ready) {
-            tc_fence_after();
-            const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
-            const uint32_t tS = tmem + 256 * g, tO = tS + 128;
-            if (d.w == KIND_L) {
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint64_t pd = smem_desc(B + kk * 2048, kHalf, 1024, kSwz128);  // P^T
-                mma_ss(tO, pd, smem_desc(A + kk * 2048, kHalf, 1024, kSwz128), id_mm, kk > 0);
-                mma_ss(tS, pd, smem_desc(ones, 128, 256, kSwzNone), id_cr, kk > 0);
-              }
-            } else if (d.w == KIND_O || part == 1) {
-              gemm2_ts<BF16>(tO, tS, A);  // out: P y_j; R-final part 2: P V[m] (tile A)
-            } else {
-              gemm2_ts<BF16>(tO, tS, B);  // R: P K[m]
-            }
-            mma_commit(bar(kBarOFull, g));
-            ++parts[g];
-            if (++part == (two ? 2 : 1)) {
-              ++n;  // the epilogue releases the entry once its stores read the tiles
-              part = 0;
-              x_ok = false;
-            }
-            progressed = true;
-          }
+      uint32_t m = 0;
+      bool ok = true;
+      for (;; ++m) {
+        const int e = m % kEntries, gm = m & 1;
+        ok = wait_bar(bar(kBarFull, e), (m / kEntries) & 1, guard);
+        if (!ok) break;
+        if (m >= *n_end_s) break;  // end marker: no item m
+        if (m >= 2) ok = wait_bar(bar(kBarG2, gm), ((m - 2) >> 1) & 1, guard);
+        if (ok && prev_kind[gm] == KIND_L) {  // its cr lives in S[gm]: wait until read
+          ok = wait_bar(bar(kBarCrTaken, gm), cr_waits[gm] & 1, guard);
+          ++cr_waits[gm];
         }
-        // ---- GEMM1 of item m ----
-        if (m < n_end && m <= n + 1) {
-          const int e = m % kEntries, gm = m & 1;
-          if (mbar_test(bar(kBarFull, e), (m / kEntries) & 1)) {
-            if (m >= *n_end_s) {
-              n_end = m;
-            } else {
-              bool ok = true;
-              if (prev_kind[gm] == KIND_L) {  // its cr lives in S[gm]: wait until read
-                ok = mbar_test(bar(kBarCrTaken, gm), cr_waits[gm] & 1);
-                if (ok) {
-                  ++cr_waits[gm];
-                  prev_kind[gm] = -1;
-                }
-              }
-              if (ok) {
-                const int kind1 = desc_slot[e].w;
-                prev_kind[gm] = kind1;
-                tc_fence_after();
-                const uint32_t A = tbase + e * kEntryBytes;
-                gemm1<BF16>(tmem + 256 * gm, A, A + kTileBytes);
-                if (kind1 != KIND_R) {  // S - cl[k] (L / output items): the ninth K step
-                  const uint32_t xa = sbase + kOffExtA, xb = sbase + kOffVec + e * kExtBytes;
-                  const uint32_t z = sbase + kOffZero;
-                  mma_ss(tmem + 256 * gm, smem_desc(xa, z - xa, 128, kSwzNone),
-                         smem_desc(xb, z - xb, 128, kSwzNone), id_ext, 1);
-                }
-                mma_commit(bar(kBarSFull, gm));
-                trace_stamp(p, m, 3, globaltimer());
-                ++m;
-                progressed = true;
-              }
-            }
-          }
+        if (!ok) break;
+        const int kind1 = desc_slot[e].w;
+        prev_kind[gm] = kind1;
+        tc_fence_after();
+        const uint32_t A = tbase + e * kEntryBytes;
+        gemm1<BF16>(tmem + 256 * gm, A, A + kTileBytes);
+        if (kind1 != KIND_R) {  // S - cl[k] (L / output items): the ninth K step
+          const uint32_t xa = sbase + kOffExtA, xb = sbase + kOffVec + e * kExtBytes;
+          const uint32_t z = sbase + kOffZero;
+          mma_ss(tmem + 256 * gm, smem_desc(xa, z - xa, 128, kSwzNone),
+                 smem_desc(xb, z - xb, 128, kSwzNone), id_ext, 1);
         }
-        if (n >= n_end) break;
-        if (progressed) {
-          t_last = globaltimer();
-        } else if ((spin & 255u) == 0) {
-          if (ld_relaxed(guard.abort)) break;
-          if (globaltimer() - t_last > guard.limit) {
-            guard.raise(MA_STATUS_WAIT_TIMEOUT);
-            break;
-          }
-        }
+        mma_commit(bar(kBarSFull, gm));
+        trace_stamp(p, m, 3, globaltimer());
       }
-      // let every issued MMA complete, then pass the end marker on: one
-      // extra phase of S-full (softmax groups) and O-full (epilogue) each
+      // let the GEMM1s complete, then pass the end marker to the softmax
+      // groups: one extra S-full phase each, posted only after the group's
+      // last real item was taken (its GEMM2 issued), so the phase cannot
+      // alias under the group's parity wait
       mma_commit(bar(kBarDrain, 0));
       const uint64_t t0 = globaltimer();
       while (!mbar_try(bar(kBarDrain, 0), 0) && globaltimer() - t0 < guard.limit) {
       }
-      if (*n_end_s == 0xFFFFFFFFu) *n_end_s = n;  // gave up: stop everyone
-      // The softmax groups have observed every S-full phase (each item's
-      // P-ready was seen before its GEMM2), so one extra phase cannot alias.
-      mbar_arrive(bar(kBarSFull, 0));
-      mbar_arrive(bar(kBarSFull, 1));
-      // The epilogue may still be draining earlier items: an extra O-full
-      // phase landing before it observed the group's last real one would
-      // advance the barrier two phases and the parity wait would miss it.
-      // Wait (bounded) until the group's last O part was released first.
+      if (*n_end_s == 0xFFFFFFFFu) *n_end_s = m;  // gave up: stop everyone
+      const uint32_t n_end = m;
       for (int g = 0; g < 2; ++g) {
-        if (parts[g] > 0) {
+        if (ok && n_end > (uint32_t)g) {
+          const uint32_t last = ((n_end - 1 - g) & ~1u) + g;  // the group's last item
           const uint64_t t1 = globaltimer();
-          while (!mbar_try(bar(kBarOFree, g), (parts[g] - 1) & 1) &&
-                 globaltimer() - t1 < guard.limit) {
+          while (!mbar_try(bar(kBarG2, g), (last >> 1) & 1) && globaltimer() - t1 < guard.limit) {
           }
         }
-        mbar_arrive(bar(kBarOFull, g));
+        mbar_arrive(bar(kBarSFull, g));
       }
     }
   } else if (warp < 8) {
@@ -570,6 +498,9 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
     const int row = tid & 127;  // = TMEM lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t tS = tmem + 256 * g + lane_off;
+    constexpr uint32_t id_mm = idesc_f16(BF16, true, true, 128, 128);  // ar = P^T Q_j
+    constexpr uint32_t id_cr = idesc_f16(BF16, true, false, 128, 16);  // cr = P^T 1
+    uint32_t g2_parts = 0;  // O parts this group committed (row 0)
     for (uint32_t k = 0;; ++k) {
       const uint32_t n = 2 * k + g;
       const int e = n % kEntries;
@@ -593,7 +524,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       const int pk_row = row / BLK;
       const int h_lo = PACK == 1 ? 0 : pk_row, h_hi = PACK == 1 ? 2 : pk_row + 1;
 
-      // late X tile (V[m] for R-final, y_j for out) into tile A, free after GEMM1
+      // late X tile (V[m] for R-final, y_j for out) into tile A, free after
+      // GEMM1; every item completes one phase of X[e] (a plain arrival when
+      // there is no late tile), so item n waits for phase n / kEntries
+      if (!(final_ || kind == KIND_O) && row == 0) mbar_arrive(bar(kBarX, e));
       if ((final_ || kind == KIND_O) && row == 0) {
         fence_proxy_async_global();
         const uint32_t xb = bar(kBarX, e);
@@ -778,6 +712,59 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       tc_fence_before();
       mbar_arrive(bar(kBarPReady, g));
       if (row == 0) trace_stamp(p, n, 5, globaltimer());
+      if (row == 0) {
+        // GEMM2 of this item, issued here as soon as its P (all 128 rows),
+        // its late X tile and the group's O accumulator are ready; then the
+        // MMA warp may reuse S of the group (kBarG2)
+        bool ok2 = wait_bar(bar(kBarPReady, g), k & 1, guard);
+        const int nparts = final_ ? 2 : 1;
+        for (int part = 0; ok2 && part < nparts; ++part) {
+          if (kind == KIND_O || part == 1) ok2 = wait_bar(bar(kBarX, e), (n / kEntries) & 1, guard);
+          if (ok2 && g2_parts > 0) ok2 = wait_bar(bar(kBarOFree, g), (g2_parts - 1) & 1, guard);
+          if (!ok2) break;
+          tc_fence_after();
+          const uint32_t tSg = tmem + 256 * g, tO = tSg + 128;
+          if (kind == KIND_L) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t pd = smem_desc(B + kk * 2048, kHalf, 1024, kSwz128);  // P^T
+              mma_ss(tO, pd, smem_desc(A + kk * 2048, kHalf, 1024, kSwz128), id_mm, kk > 0);
+              mma_ss(tSg, pd, smem_desc(sbase + kOffOnes, 128, 256, kSwzNone), id_cr, kk > 0);
+            }
+          } else if (kind == KIND_O || part == 1) {
+            gemm2_ts<BF16>(tO, tSg, A);  // out: P y_j; R-final part 2: P V[m] (tile A)
+          } else {
+            gemm2_ts<BF16>(tO, tSg, B);  // R: P K[m]
+          }
+          mma_commit(bar(kBarOFull, g));
+          ++g2_parts;
+        }
+        // (a failed wait leaves through the abort flag at the group's next
+        // warp-uniform wait, so the warp's lanes stay together)
+        if (ok2) {
+          tc_fence_before();
+          mbar_arrive(bar(kBarG2, g));
+        }
+      }
+    }
+    if (row == 0) {
+      // The epilogue may still be draining this group's last item: post the
+      // end marker on O-full only after its last real phase was released
+      // (else the barrier would advance two phases under its parity wait),
+      // and never leave with issued MMAs running.
+      if (!ld_relaxed(guard.abort)) {
+        if (g2_parts > 0) {
+          const uint64_t t1 = globaltimer();
+          while (!mbar_try(bar(kBarOFree, g), (g2_parts - 1) & 1) &&
+                 globaltimer() - t1 < guard.limit) {
+          }
+        }
+        mbar_arrive(bar(kBarOFull, g));
+      }
+      mma_commit(bar(kBarDrain2, g));
+      const uint64_t t2 = globaltimer();
+      while (!mbar_try(bar(kBarDrain2, g), 0) && globaltimer() - t2 < guard.limit) {
+      }
     }
   } else if (warp < kEpiWarp0 + 4) {
     // ===================== epilogue (warpgroup 2) =====================
