@@ -179,14 +179,14 @@ template <bool BF16>
 __device__ __forceinline__ void stage_row128(uint32_t tile, int row, uint32_t taddr, float scale) {
   uint32_t ca[16], cb[16];
   const uint32_t rbase = tile + row * 128;
+  const uint64_t sc2 = f2pack(scale, scale);
   auto put = [&](const uint32_t(&cv)[16], int ch) {
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       uint32_t w[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        w[q] = pack2<BF16>(__uint_as_float(cv[8 * t + 2 * q]) * scale,
-                           __uint_as_float(cv[8 * t + 2 * q + 1]) * scale);
+        w[q] = scale_pack2<BF16>(cv[8 * t + 2 * q], cv[8 * t + 2 * q + 1], sc2);
       const int u = 2 * ch + t;
       st_shared_v4(rbase + (u >> 3) * kHalf + (((u & 7) ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
     }
@@ -683,14 +683,14 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         // chunk ch = two 16-byte units (8 columns each) of the row: unit
         // u = 2 ch + t of the 128-column row sits in half u / 8, position
         // (u % 8) ^ (row % 8)
+        const uint64_t so2 = f2pack(scale_out, scale_out);
         auto st_chunk = [&](const uint32_t(&cv)[16], int ch) {
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
             uint32_t a[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              a[q] = pack2<BF16>(__uint_as_float(cv[8 * t + 2 * q]) * scale_out,
-                                 __uint_as_float(cv[8 * t + 2 * q + 1]) * scale_out);
+              a[q] = scale_pack2<BF16>(cv[8 * t + 2 * q], cv[8 * t + 2 * q + 1], so2);
             const int u = 2 * ch + t;
             st_shared_v4(prow + (u >> 3) * kHalf + (((u & 7) ^ (row & 7)) << 4), a[0], a[1], a[2],
                          a[3]);

@@ -111,14 +111,14 @@ __device__ __forceinline__ void stage_row(uint32_t tile, uint32_t hstride, int r
                                           float scale) {
   uint32_t ca[16], cb[16];
   const uint32_t rbase = tile + row * 128;
+  const uint64_t sc2 = f2pack(scale, scale);
   auto put = [&](const uint32_t(&cv)[16], int ch) {
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       uint32_t w[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q)
-        w[q] = pack2<BF16>(__uint_as_float(cv[8 * t + 2 * q]) * scale,
-                           __uint_as_float(cv[8 * t + 2 * q + 1]) * scale);
+        w[q] = scale_pack2<BF16>(cv[8 * t + 2 * q], cv[8 * t + 2 * q + 1], sc2);
       const int u = 2 * ch + t;
       st_shared_v4(rbase + (u >> 3) * hstride + (((u & 7) ^ (row & 7)) << 4), w[0], w[1], w[2],
                    w[3]);

@@ -280,6 +280,11 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -293,6 +298,13 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   else
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+// two fp32 values times a common scale, packed into one 16-bit pair
+template <bool BF16>
+__device__ __forceinline__ uint32_t scale_pack2(uint32_t lo, uint32_t hi, uint64_t sc2) {
+  float a, b;
+  f2unpack(fmul2(f2pack(__uint_as_float(lo), __uint_as_float(hi)), sc2), a, b);
+  return pack2<BF16>(a, b);
 }
 __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, uint32_t c,
                                              uint32_t d) {
