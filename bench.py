@@ -5,14 +5,17 @@
 
 One step = one MonarchAttention forward over the configuration's whole batch
 (default: the north-star config, E=4 H=16 N=16384 d=128 b=128 T=2 bf16).
-Under torchrun each rank runs its own full copy of the workload on its own GPU
-with its own seed (batch x heads sharded across GPUs, no collective on the
-data path): weak scaling, value = all ranks' tokens / max-over-ranks time.
+Under torchrun the E*H heads of that ONE workload are split across the ranks
+(contiguous ranges, whole batch rows when E is a multiple of the rank count;
+every (e, h) is independent, so there is no collective on the data path):
+strong scaling, value = the workload's tokens / max-over-ranks time.  After
+timing, the output shards are all-gathered over NCCL and rank 0 checks them
+bit for bit against its own single-GPU forward of the whole workload.
 
 ``--impl reference`` times the reference algorithm on the host CPU instead:
 the reference is Python (ma/ma_torch.py) and cannot be installed on the GPU
 box, so its CPU restatement in oracle/ma_oracle.py runs on all host cores
-(rank 0 only), on a bounded sample of heads per step.
+(rank 0 only) over every head of the workload in every step.
 """
 from __future__ import annotations
 
@@ -47,8 +50,6 @@ def parse():
                     help="target CPU time of the cpu_baseline sample")
     ap.add_argument("--E", type=int, default=None, help="override the batch size (profiling)")
     ap.add_argument("--H", type=int, default=None, help="override the head count (profiling)")
-    ap.add_argument("--verify", action="store_true",
-                    help="after timing, gather outputs to rank 0 (NCCL) and check heads")
     return ap.parse_args()
 
 
@@ -124,28 +125,30 @@ def cpu_rate(cfg, threads, target_s, first_heads=None):
 
 
 def run_reference(args, cfg, rank, world):
+    """The reference arm: every step runs the oracle port over ALL E*H heads of
+    the workload on the host cores (no sampling, no extrapolation)."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    heads = min(threads, cfg.E * cfg.H)
+    heads = cfg.E * cfg.H
     inputs = cpu_inputs(cfg, heads)
     for _ in range(args.warmup):
         cpu_sample(cfg, heads, threads, inputs)
     times = []
     for _ in range(args.steps):
         times.append(cpu_sample(cfg, heads, threads, inputs))
-    per_step_sample = sum(times) / len(times)
-    full_step = per_step_sample * (cfg.E * cfg.H) / heads
+    step = sum(times) / len(times)
     tokens = cfg.E * cfg.N
-    value = tokens / full_step
-    sample = (f"{heads} of {cfg.E * cfg.H} (e,h) heads per step on {threads} host threads "
-              f"({cfg.dtype} emulated by the oracle port), scaled to the full batch")
+    value = tokens / step
+    sample = (f"every step: all {heads} (e,h) heads of {cfg.name} on {threads} host threads "
+              f"(oracle port of ma/ma_torch.py, {cfg.dtype} rounding emulated), "
+              f"{args.steps} timed steps")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": full_step * 1e3, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
-        "config": config_dict(cfg),
+        "ms_per_step": step * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic (seeded iid normal)",
+        "config": config_dict(cfg, max(world, args.gpus)),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -157,13 +160,39 @@ def run_reference(args, cfg, rank, world):
 # ---------------------------------------------------------------------------
 # GPU leg
 # ---------------------------------------------------------------------------
-def config_dict(cfg, extra=None):
-    d = {"workload": cfg.name, "E": cfg.E, "H": cfg.H, "N": cfg.N, "D": cfg.D, "Dv": cfg.dv,
-         "block_size": cfg.B, "num_steps": cfg.T, "mask": cfg.mask_min_len is not None,
-         "pre_pad": cfg.pre_pad}
-    if extra:
-        d.update(extra)
-    return d
+def input_bytes(cfg):
+    in_b = {"f32": 4, "f16": 2, "bf16": 2, "e4m3": 1}[cfg.dtype]
+    return cfg.E * cfg.H * cfg.N * (2 * cfg.D + cfg.dv) * in_b
+
+
+def shard_input_bytes(cfg, world):
+    """Input bytes of the largest per-GPU shard at `world` GPUs."""
+    from monarch_attention_b200.shard import shard_range
+    most = max(b - a for a, b in (shard_range(cfg.E, cfg.H, world, r) for r in range(world)))
+    return input_bytes(cfg) * most // (cfg.E * cfg.H)
+
+
+def needs_flush(cfg, world):
+    """Per-GPU inputs smaller than 2x L2 could stay cached between steps."""
+    return shard_input_bytes(cfg, world) < 2 * L2_BYTES
+
+
+def l2_note(cfg, world):
+    """How the GPU arm keeps L2 from carrying inputs between timed steps (a
+    property of the workload and the GPU count; identical in both arms)."""
+    mib = shard_input_bytes(cfg, world) / 2**20
+    if needs_flush(cfg, world):
+        return (f"per-GPU inputs {mib:.0f} MiB < 2x L2: L2 flushed between timed steps "
+                "(256 MB write, outside the events)")
+    return f"per-GPU inputs {mib:.0f} MiB, larger than 2x the 126 MiB L2 (no flush)"
+
+
+def config_dict(cfg, world):
+    """The workload (identical in the GPU arm and the reference arm)."""
+    return {"workload": cfg.name, "E": cfg.E, "H": cfg.H, "N": cfg.N, "D": cfg.D,
+            "Dv": cfg.dv, "block_size": cfg.B, "num_steps": cfg.T,
+            "mask": cfg.mask_min_len is not None, "pre_pad": cfg.pre_pad, "dtype": cfg.dtype,
+            "l2": l2_note(cfg, world)}
 
 
 class ClockSampler:
@@ -250,6 +279,7 @@ def run_gpu(args, cfg, rank, world, local_rank):
     import monarch_attention_b200 as mab
     from monarch_attention_b200 import _lib
     from monarch_attention_b200.configs import make_inputs
+    from monarch_attention_b200.shard import gather_shards, shard_problem
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -263,10 +293,17 @@ def run_gpu(args, cfg, rank, world, local_rank):
             dist.barrier()
         torch.cuda.synchronize()
 
-    # every rank owns its own shard of batch x heads (its own seed)
-    q, k, v, mask, scales = make_inputs(cfg, device=dev, seed=cfg.seed + 7919 * rank)
+    # ONE workload for every world size (same seed on every rank; the CUDA
+    # generator gives the same numbers on every device), split by heads
+    fq, fk, fv, fmask, fscales = make_inputs(cfg, device=dev)
+    q, k, v, mask, scales, (h0, h1) = shard_problem(fq, fk, fv, fmask, fscales, world, rank)
+    keep_full = world > 1 and rank == 0  # rank 0 re-runs the whole workload to verify
+    if not keep_full:
+        fq = fk = fv = fmask = fscales = None
+    torch.cuda.empty_cache()
     impl = args.kernel
-    out = torch.empty((cfg.E, cfg.H, cfg.N, cfg.dv),
+    Eh, Hh = q.shape[0], q.shape[1]
+    out = torch.empty((Eh, Hh, cfg.N, cfg.dv),
                       dtype=torch.bfloat16 if cfg.dtype == "e4m3" else q.dtype, device=dev)
     kernel_family = mab.selected_impl(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, impl=impl)
 
@@ -274,8 +311,9 @@ def run_gpu(args, cfg, rank, world, local_rank):
         return mab.monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, impl=impl,
                                      scales=scales, out=out)
 
-    in_bytes = sum(t.numel() * t.element_size() for t in (q, k, v))
-    flush = in_bytes < 2 * L2_BYTES
+    # flush when the largest per-GPU shard could stay in L2 (the same decision
+    # on every rank)
+    flush = needs_flush(cfg, world)
     scrub = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
 
     stream = torch.cuda.current_stream(dev)
@@ -312,7 +350,7 @@ def run_gpu(args, cfg, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_total = float(t.item())
     ms_step = ms_total / args.steps
-    tokens_step = cfg.E * cfg.N * world
+    tokens_step = cfg.E * cfg.N  # the whole workload, whatever the rank count
     value = tokens_step / (ms_step / 1e3)
 
     # ---- end to end through the public API: host (pinned) -> device -> host.
@@ -320,6 +358,7 @@ def run_gpu(args, cfg, rank, world, local_rank):
     # region; the copies run on their own streams with two buffer sets, so
     # step i+1's input copy and step i-1's result copy overlap step i's
     # forward (a serving pipeline; PCIe carries both directions at once).
+    # Each rank copies its own shard over its own link.
     e2e = None
     if not args.no_e2e:
         hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
@@ -379,24 +418,43 @@ def run_gpu(args, cfg, rank, world, local_rank):
         h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv))
         h2d += 0 if hm is None else hm.numel() * hm.element_size()
         h2d += 0 if hsc is None else sum(x.numel() * x.element_size() for x in hsc)
+        d2h = hout[0].numel() * hout[0].element_size()
+        if world > 1:  # whole-job bytes: the sum over ranks
+            tb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+            dist.all_reduce(tb)
+            h2d, d2h = int(tb[0].item()), int(tb[1].item())
         e2e = {"value": tokens_step / (e2e_ms / 1e3), "unit": "tokens/s",
                "ms_per_step": e2e_ms, "steps": n_e2e, "pipelined": "double-buffered copy streams",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": hout[0].numel() * hout[0].element_size()}
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        del hq, hk, hv, hm, hout, dbuf, dm, dsc, dout
 
+    # ---- verification (after timing): NCCL all-gather of the output shards;
+    # rank 0 compares them bit for bit with its own forward of the whole
+    # workload on one GPU (a head's result does not depend on which heads
+    # share its launch)
     verify = None
-    if args.verify and world > 1:
-        # every rank's output shard over NCCL to every rank (after timing);
-        # rank 0 checks the shards are finite and that its own came back intact
-        gathered = [torch.empty_like(out) for _ in range(world)]
-        dist.all_gather(gathered, out)
-        torch.cuda.synchronize()
-        verify = {"gathered_bytes": sum(t.numel() * t.element_size() for t in gathered),
-                  "all_finite": bool(all(torch.isfinite(t).all().item() for t in gathered)),
-                  "own_shard_equal": bool(torch.equal(gathered[rank], out))}
+    if world > 1:
+        from monarch_attention_b200.shard import shard_range
+        full = gather_shards(out, cfg.E, cfg.H)
+        if rank == 0:
+            ref = mab.monarch_attention(fq, fk, fv, fmask, cfg.T, cfg.B, cfg.pre_pad, impl=impl,
+                                        scales=fscales)
+            torch.cuda.synchronize()
+            fl = full.reshape(cfg.E * cfg.H, cfg.N, cfg.dv)
+            ref = ref.reshape(cfg.E * cfg.H, cfg.N, cfg.dv)
+            sizes = [shard_range(cfg.E, cfg.H, world, r) for r in range(world)]
+            same = [bool(torch.equal(fl[a:b], ref[a:b])) for a, b in sizes]
+            verify = {"heads": cfg.E * cfg.H, "gathered_bytes": full.numel() * full.element_size(),
+                      "bit_exact_per_rank": same, "all_bit_exact": all(same),
+                      "all_finite": bool(torch.isfinite(full.float()).all().item()),
+                      "status": mab.read_status(dev)}
+            del ref, fl
+        del full
+        barrier()
 
     # ---- roofline of the dominant kernel (one forward = one launch on tc)
     peaks, peak_src = load_peaks()
-    flop, byts = flops_and_bytes(cfg)
+    flop, byts = flops_and_bytes(cfg)  # the whole workload (all ranks)
     t_s = ms_step / 1e3
     if cfg.dtype == "f32":
         peak_flops = 148 * 128 * 2 * 1.965e9
@@ -404,7 +462,8 @@ def run_gpu(args, cfg, rank, world, local_rank):
     else:
         peak_flops = peaks["bf16_tflops"] * 1e12 * (2 if cfg.dtype == "e4m3" else 1)
         peak_note = f"bf16 dense burst, {peak_src}" + (" x2 (fp8 assumed)" if cfg.dtype == "e4m3" else "")
-    hbm = peaks["hbm_gbs"] * 1e9
+    peak_flops *= world
+    hbm = peaks["hbm_gbs"] * 1e9 * world
     t_flop, t_hbm = flop / peak_flops, byts / hbm
     if t_flop >= t_hbm:
         roof = {"bound": "tensor", "achieved": flop / t_s / 1e12, "peak": peak_flops / 1e12,
@@ -412,32 +471,35 @@ def run_gpu(args, cfg, rank, world, local_rank):
     else:
         roof = {"bound": "hbm", "achieved": byts / t_s / 1e9, "peak": hbm / 1e9, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["peak_source"] = peak_note if roof["bound"] == "tensor" else f"hbm copy, {peak_src}"
-    roof["traffic"] = load_traffic(cfg.name, kernel_family)
+    roof["peak_source"] = (peak_note if roof["bound"] == "tensor" else f"hbm copy, {peak_src}") + \
+        (f", x {world} GPUs" if world > 1 else "")
+    traffic = load_traffic(cfg.name, kernel_family)
+    roof["traffic"] = None if traffic is None else traffic / world  # per launch (one rank's)
     roof["t_star_us"] = max(t_flop, t_hbm) * 1e6
-    roof["algorithmic_flop_per_launch"] = flop
-    roof["algorithmic_bytes_per_launch"] = byts
+    roof["algorithmic_flop_per_launch"] = flop / world
+    roof["algorithmic_bytes_per_launch"] = byts / world
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         rate, heads, secs = cpu_rate(cfg, threads, args.cpu_seconds)
-        full = (cfg.E * cfg.H) / rate
-        cpu = {"value": cfg.E * cfg.N / full, "unit": "tokens/s", "cores": threads,
+        full_s = (cfg.E * cfg.H) / rate
+        cpu = {"value": cfg.E * cfg.N / full_s, "unit": "tokens/s", "cores": threads,
                "kind": "port",
-               "sample": f"{heads} (e,h) heads of {cfg.name} in {secs:.1f} s on {threads} "
-                         f"host threads (oracle port of ma/ma_torch.py), scaled to the batch"}
+               "sample": f"{heads} of the {cfg.E * cfg.H} (e,h) heads of {cfg.name} in "
+                         f"{secs:.1f} s on {threads} host threads (oracle port of "
+                         f"ma/ma_torch.py), per-head rate scaled to the batch"}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": cfg.dtype, "data": "synthetic (seeded iid normal, per-rank seed)",
-            "config": config_dict(cfg, {
-                "kernel": kernel_family, "parallelism": f"batch x heads over {world} GPU(s)",
-                "l2": ("L2 flushed between timed steps (256 MB write, outside the events)"
-                       if flush else f"inputs larger than L2 ({in_bytes / 2**20:.0f} MiB)")}),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": cfg.dtype, "data": "synthetic (seeded iid normal)",
+            "config": config_dict(cfg, world),
+            "kernel": kernel_family,
+            "parallelism": (f"E*H = {cfg.E * cfg.H} heads split over {world} GPU(s), "
+                            f"{h1 - h0} heads on rank 0; no collective on the data path"),
             "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
             "gpu_launches": launches_per_fwd * args.steps, "clocks": clk,
             "device_status": status,

@@ -35,7 +35,7 @@
 extern "C" {
 #endif
 
-#define MA_API_VERSION 1
+#define MA_API_VERSION 2
 
 /* Element types of q / k / v / out. */
 typedef enum {
@@ -119,10 +119,22 @@ typedef struct {
   size_t workspace_bytes;
   uint32_t* status; /* device word; bits MA_STATUS_* are OR-ed in          */
   int32_t impl;     /* ma_impl_t                                          */
-  int32_t reserved[7];
+  int32_t reserved0;
+  /* optional (NULL = none): a word of page-locked host memory that the
+   * device can write (cudaHostAlloc / cudaMallocHost, same address on host
+   * and device).  A kernel that sets a status bit also stores that bit here
+   * with a plain store, so the host sees "a failure happened" without a
+   * device read; the exact bits stay in *status.  Nothing is written on
+   * success.  (API version 2; older callers leave it zero.)               */
+  uint32_t* status_host;
+  int32_t reserved[4];
 } ma_fwd_params;
 
-/* Bytes of workspace ma_fwd() needs for these params (0 on bad params). */
+/* Bytes of workspace ma_fwd() needs for these params (0 on bad params).
+ * The size depends on the kernel ma_fwd() selects (the persistent tcgen05
+ * kernel cycles through a few head slots only), so pass the same params,
+ * pointers included, that ma_fwd() will get; a workspace that is too small
+ * for the kernel actually selected is rejected with MA_ERR_WORKSPACE. */
 size_t ma_workspace_bytes(const ma_fwd_params* p);
 
 /* Enqueue one MonarchAttention forward on `stream`
@@ -134,8 +146,7 @@ int ma_fwd(const ma_fwd_params* p, void* stream);
  * serving loop with a fixed device-memory budget where an allocation could
  * block or fail): the scratch comes from a 64 MiB
  * array compiled into the library instead of p->workspace, which is ignored.
- * No counterpart in the reference (its PyTorch implementation allocates its
- * intermediates per call, ma/ma_torch.py:89).
+ * This entry point has no counterpart in the reference.
  *   - Runs the persistent tcgen05 kernel only: head dim 128, block size =
  *     number of blocks = 64 or 128, bf16 / fp16, no mask; other shapes, and
  *     shapes whose scratch exceeds 64 MiB, return MA_ERR_UNSUPPORTED before

@@ -9,6 +9,7 @@ from .monarch_attention import (
     MonarchAttention,
     PadType,
     build_params,
+    check_status,
     monarch_attention,
     read_status,
     selected_impl,
@@ -20,6 +21,7 @@ __all__ = [
     "MonarchAttentionError",
     "PadType",
     "build_params",
+    "check_status",
     "lib_path",
     "load_library",
     "monarch_attention",

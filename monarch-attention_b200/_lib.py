@@ -23,6 +23,8 @@ IMPL_NAMES = {IMPL_GENERIC: "generic", IMPL_TC: "tc", IMPL_SMALL: "small"}
 
 MA_OK = 0
 MA_ERR_INJECTED = 8
+MA_ERR_BAD_PARAMS = 9
+MA_ERR_DEVICE = -2
 MA_STATUS_WAIT_TIMEOUT = 0x1
 MA_STATUS_TMEM_FAIL = 0x2
 MA_STATUS_BAD_ITEM = 0x4
@@ -74,7 +76,9 @@ class MaFwdParams(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("status", ctypes.c_void_p),
         ("impl", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 7),
+        ("reserved0", ctypes.c_int32),
+        ("status_host", ctypes.c_void_p),
+        ("reserved", ctypes.c_int32 * 4),
     ]
 
     def __init__(self, **kw):

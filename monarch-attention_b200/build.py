@@ -46,24 +46,46 @@ def up_to_date() -> bool:
 
 def build(force: bool = False, verbose: bool = False, out: str = OUT,
           defines: tuple = ()) -> str:
-    """Compile every .cu under csrc/ into libmonarch_attn.so; returns its path.
+    """Compile every .cu under csrc/ (one nvcc per file, in parallel) and link
+    libmonarch_attn.so; returns its path.
 
     ``defines`` adds -D flags (e.g. ("MA_TC_TRACE",) for the per-item timeline
     build, written to a separate ``out`` path).
     """
     if not force and out == OUT and up_to_date():
         return out
-    tmp = out + ".tmp"
-    cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, *[f"-D{d}" for d in defines], "-I", INCLUDE,
-           "-o", tmp, *sources()]
-    res = subprocess.run(cmd, capture_output=True, text=True)
+    from concurrent.futures import ThreadPoolExecutor
+    import tempfile
+    objdir = tempfile.mkdtemp(prefix="ma_build_")
+    dflags = [f"-D{d}" for d in defines]
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+
+    def compile_one(src):
+        obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
+        cmd = [nvcc(), *ARCH_FLAGS, *compile_flags, *dflags, "-I", INCLUDE, "-c", "-o", obj, src]
+        return obj, cmd, subprocess.run(cmd, capture_output=True, text=True)
+
+    srcs = sources()
+    with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 1)) as ex:
+        results = list(ex.map(compile_one, srcs))
     log = os.path.join(HERE, "build.log")
+    tmp = out + ".tmp"
+    link = [nvcc(), *ARCH_FLAGS, "-shared", "-o", tmp, *[r[0] for r in results]]
     with open(log, "w") as f:
-        f.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+        for obj, cmd, res in results:
+            f.write(" ".join(cmd) + "\n" + res.stdout + res.stderr)
+        bad = [r for r in results if r[2].returncode != 0]
+        if bad:
+            shutil.rmtree(objdir, ignore_errors=True)
+            raise RuntimeError(f"nvcc failed (see {log}):\n" +
+                               "\n".join(r[2].stderr[-4000:] for r in bad))
+        res = subprocess.run(link, capture_output=True, text=True)
+        f.write(" ".join(link) + "\n" + res.stdout + res.stderr)
+    shutil.rmtree(objdir, ignore_errors=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed (see {log}):\n{res.stderr[-4000:]}")
+        raise RuntimeError(f"link failed (see {log}):\n{res.stderr[-4000:]}")
     if verbose:
-        print(res.stderr)
+        print(open(log).read())
     os.replace(tmp, out)
     return out
 

@@ -31,6 +31,7 @@ cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
                       cudaStream_t st, int* nlaunch);
 // ma_tc.cu
 bool tc_supports(const ma_fwd_params* p, const Shape& s);
+int tc_slots(const Shape& s);
 size_t tc_ctrl_bytes(const Shape& s);
 cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, cudaStream_t st,
                    int* nlaunch);
@@ -42,6 +43,22 @@ namespace {
 
 thread_local std::string g_detail;
 thread_local int g_launches = 0;
+thread_local const void* g_host_word_ok = nullptr;  // last status_host that passed
+
+// A status_host word must be page-locked host memory mapped into the device
+// address space at the same address (what cudaHostAlloc / cudaMallocHost
+// give with unified addressing).
+bool host_word_ok(const void* ptr) {
+  if (ptr == g_host_word_ok) return true;
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  if (a.type != cudaMemoryTypeHost || a.devicePointer != ptr) return false;
+  g_host_word_ok = ptr;
+  return true;
+}
 
 int fail(int code, const std::string& detail) {
   g_detail = detail;
@@ -71,12 +88,18 @@ Shape make_shape(const ma_fwd_params* p) {
   return s;
 }
 
-// conv: reserve bf16 copies of e4m3 q / k / v (tensor-core kernels)
-WsLayout make_layout(const Shape& s, int dtype, bool conv) {
+// Workspace layout for the kernel family `impl` (MA_IMPL_*).  conv: reserve
+// bf16 copies of e4m3 q / k / v (tensor-core kernels).  The persistent
+// tcgen05 kernel (b = 64, 128) cycles through tc_slots() head slots of the
+// al / y / ar / cl / cr arrays and needs no lmax / lsum; every other kernel
+// keeps the arrays of all E * H heads.
+WsLayout make_layout(const Shape& s, int dtype, bool conv, int impl) {
   WsLayout w{};
   // intermediates are kept in the input precision; e4m3 inputs use bf16
   w.store_bytes = dtype == MA_DTYPE_F32 ? 4 : 2;
-  const size_t heads = (size_t)s.E * s.H;
+  const bool tc_shape = s.D == 128 && s.b == s.M && (s.b == 64 || s.b == 128 || s.b == 256);
+  const bool persistent = impl == MA_IMPL_TC && tc_shape && s.b != 256;
+  const size_t heads = persistent ? (size_t)tc_slots(s) : (size_t)s.E * s.H;
   const size_t bm = (size_t)s.b * s.M;
   size_t off = 0;
   w.al = off; off = align_up(off + heads * bm * s.D * w.store_bytes, 256);
@@ -84,20 +107,21 @@ WsLayout make_layout(const Shape& s, int dtype, bool conv) {
   w.ar = off; off = align_up(off + heads * bm * s.D * w.store_bytes, 256);
   w.cl = off; off = align_up(off + heads * bm * 4, 256);
   w.cr = off; off = align_up(off + heads * bm * 4, 256);
-  if (s.D == 128 && s.b == s.M && (s.b == 64 || s.b == 128 || s.b == 256)) {  // tcgen05 shapes
+  if (tc_shape) {
     w.clx = off; off = align_up(off + heads * bm * 16, 256);
     if (s.b == 256) {
       w.lsex = off; off = align_up(off + heads * bm * 16, 256);
     }
   }
-  w.lmax = off; off = align_up(off + heads * bm * 4, 256);
-  w.lsum = off; off = align_up(off + heads * bm * 4, 256);
+  const size_t lrows = persistent ? 0 : heads * bm;
+  w.lmax = off; off = align_up(off + lrows * 4, 256);
+  w.lsum = off; off = align_up(off + lrows * 4, 256);
   w.ctrl = off;
   w.ctrl_bytes = tc_ctrl_bytes(s);
   w.tc_slots = (int)heads;
   off = align_up(off + w.ctrl_bytes, 256);
   if (conv) {
-    const size_t rows = heads * (size_t)s.N;
+    const size_t rows = (size_t)s.E * s.H * (size_t)s.N;
     w.xq = off; off = align_up(off + rows * s.D * 2, 256);
     w.xk = off; off = align_up(off + rows * s.D * 2, 256);
     w.xv = off; off = align_up(off + rows * s.Dv * 2, 256);
@@ -154,6 +178,10 @@ int validate(const ma_fwd_params* p, bool need_buffers) {
   if (!need_buffers) return MA_OK;
   if (!p->q || !p->k || !p->v || !p->out) return fail(MA_ERR_NULL_POINTER, "q/k/v/out is NULL");
   if (!p->status) return fail(MA_ERR_NULL_POINTER, "status word is NULL");
+  if (p->status_host && !host_word_ok(p->status_host))
+    return fail(MA_ERR_BAD_PARAMS,
+                "status_host is not page-locked host memory the device can write at the "
+                "same address");
   if (p->dtype == MA_DTYPE_E4M3 && (!p->q_scale || !p->k_scale || !p->v_scale))
     return fail(MA_ERR_NULL_POINTER, "e4m3 inputs need q/k/v scales");
   const int64_t* st[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
@@ -220,27 +248,24 @@ int select_impl(const ma_fwd_params* p, const Shape& s, int* impl) {
 }  // namespace
 
 namespace ma {
-// Lets the allocation-free entry point (ma_noalloc.cu) report through
-// ma_last_error_detail().
+// Let the allocation-free entry point (ma_noalloc.cu) report through
+// ma_last_error_detail() and ma_last_launch_count().
 void set_error_detail(const std::string& detail) { g_detail = detail; }
+void set_launch_count(int n) { g_launches = n; }
 }  // namespace ma
 
 extern "C" {
 
-// e4m3 calls that run on a tensor-core kernel need the bf16 copies
-bool needs_conversion(const ma_fwd_params* p, const Shape& s) {
-  if (p->dtype != MA_DTYPE_E4M3) return false;
-  int impl = 0;
-  const std::string keep = g_detail;
-  const bool ok = select_impl(p, s, &impl) == MA_OK;
-  g_detail = keep;
-  return ok && impl != MA_IMPL_GENERIC;
-}
-
 size_t ma_workspace_bytes(const ma_fwd_params* p) {
   if (validate(p, false) != MA_OK) return 0;
   const Shape s = make_shape(p);
-  return make_layout(s, p->dtype, needs_conversion(p, s)).total;
+  int impl = 0;
+  const std::string keep = g_detail;
+  const int rc = select_impl(p, s, &impl);
+  g_detail = keep;
+  if (rc != MA_OK) return 0;
+  const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
+  return make_layout(s, p->dtype, conv, impl).total;
 }
 
 int ma_select_impl(const ma_fwd_params* p) {
@@ -262,7 +287,7 @@ int ma_fwd(const ma_fwd_params* p, void* stream) {
   rc = select_impl(p, s, &impl);
   if (rc != MA_OK) return rc;
   const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
-  const WsLayout ws = make_layout(s, p->dtype, conv);
+  const WsLayout ws = make_layout(s, p->dtype, conv, impl);
   if (p->workspace == nullptr || p->workspace_bytes < ws.total)
     return fail(MA_ERR_WORKSPACE, "workspace needs " + std::to_string(ws.total) + " bytes, got " +
                                       std::to_string(p->workspace_bytes));

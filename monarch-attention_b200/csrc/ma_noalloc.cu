@@ -37,6 +37,7 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
                    int* nlaunch);
 // ma_api.cu
 void set_error_detail(const std::string& detail);
+void set_launch_count(int n);
 }  // namespace ma
 
 namespace {
@@ -108,14 +109,15 @@ ma::WsLayout compact_layout(const ma::Shape& s, int slots, size_t* status_off) {
 }  // namespace
 
 extern "C" int ma_fwd_noalloc(const ma_fwd_params* p, void* stream) {
+  ma::set_error_detail("");
   const int sel = ma_select_impl(p);  // validates the parameter block
   if (sel < 0) return -sel;
   // e4m3 inputs reach the tcgen05 kernel only through bf16 copies in a
   // caller workspace, which this entry point does not have
   if (sel != MA_IMPL_TC || (p->dtype != MA_DTYPE_BF16 && p->dtype != MA_DTYPE_F16)) {
     ma::set_error_detail(
-        "ma_fwd_noalloc runs the tcgen05 kernel only (block size = blocks = head dim = 128, "
-        "bf16/fp16, no mask); use ma_fwd for this shape");
+        "ma_fwd_noalloc runs the persistent tcgen05 kernel only (block size = number of "
+        "blocks = 64 or 128, head dim 128, bf16/fp16, no mask); use ma_fwd for this shape");
     return MA_ERR_UNSUPPORTED;
   }
   if (!p->q || !p->k || !p->v || !p->out) {
@@ -154,5 +156,6 @@ extern "C" int ma_fwd_noalloc(const ma_fwd_params* p, void* stream) {
     ma::set_error_detail(std::string("CUDA error: ") + cudaGetErrorName(err));
     return MA_ERR_CUDA;
   }
+  ma::set_launch_count(n);
   return MA_OK;
 }

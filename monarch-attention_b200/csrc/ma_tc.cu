@@ -45,6 +45,7 @@
 //   epilogue: TMEM -> registers -> scale -> 16-bit -> global
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -137,12 +138,17 @@ struct TcParams {
   float* cr;
   uint32_t* ctrl;
   uint32_t* status;
+  uint32_t* status_host;  // host mirror of the status word (optional)
   int H, nheads, T, P, slots;
   int hgroup;  // heads per wavefront phase slot (round r runs phase p of heads hgroup*(r-p) + i)
   int early;   // 1: claim the next item (and await its dependency) before its ring entry frees
   int claim;   // items claimed per global atomic
   float sm_scale;
   unsigned long long timeout_ns;
+  // test hook (MA_TEST_STALL_DEP=head,phase): the dependency wait of that
+  // (head, phase) needs one more completed tile than the phase before it
+  // has, so it runs out after timeout_ns; -1 = off
+  int stall_head, stall_phase;
   unsigned long long* trace;  // MA_TC_TRACE builds: per-CTA item timestamps, else null
 };
 
@@ -243,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   uint32_t* ctrl = p.ctrl;
-  const Guard guard{ctrl + kCtrlAbort, p.status, p.timeout_ns};
+  const Guard guard{ctrl + kCtrlAbort, p.status, p.timeout_ns, p.status_host};
   const int P = p.P;
   const uint32_t total = (uint32_t)p.nheads * P * kTiles;
 
@@ -358,11 +364,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           // dependency: the previous phase of this head, or -- for phase 0 --
           // the output phase of the head that used this workspace slot before
           if (head != dep_head || ph != dep_ph) {
+            const uint32_t need =
+                (uint32_t)kTiles + (head == p.stall_head && ph == p.stall_phase ? 1u : 0u);
             if (ph > 0)
-              ok = wait_counter(ctrl + kCtrlDone + head * P + ph - 1, (uint32_t)kTiles, guard);
+              ok = wait_counter(ctrl + kCtrlDone + head * P + ph - 1, need, guard);
             else if (head >= p.slots)
-              ok = wait_counter(ctrl + kCtrlDone + (head - p.slots) * P + P - 1, (uint32_t)kTiles,
-                                guard);
+              ok = wait_counter(ctrl + kCtrlDone + (head - p.slots) * P + P - 1, need, guard);
             if (ok) {
               dep_head = head;
               dep_ph = ph;
@@ -961,6 +968,32 @@ bool tc_supports(const ma_fwd_params* p, const Shape& s) {
   return true;
 }
 
+// Heads per wavefront phase slot of the persistent kernel: more heads in
+// flight give a longer distance between dependent items (a round is
+// 2T * hgroup * tiles items).  Measured best on B200 for b = 128 (1: 856 us,
+// 2: 785 us, 3: 808 us, 4: 803 us); the same round length (1024 tiles) for
+// b = 64.  MA_TC_GROUP overrides it.
+int tc_hgroup(const Shape& s) {
+  const int nheads = s.E * s.H;
+  const int tiles = s.b * s.b / tc::kT;  // 128 for b = 128, 32 for b = 64
+  int hgroup = 256 / tiles;
+  const char* hg = getenv("MA_TC_GROUP");
+  if (hg) hgroup = atoi(hg);
+  if (hgroup < 1) hgroup = 1;
+  if (hgroup > nheads) hgroup = nheads;
+  return hgroup;
+}
+
+// Workspace head slots the persistent kernel cycles through: a slot is
+// reused by head h + slots once head h's output phase is done, so a group of
+// hgroup heads needs hgroup * (2T + 1) slots for every dependency to point
+// to an earlier round of the wavefront.
+int tc_slots(const Shape& s) {
+  const int nheads = s.E * s.H;
+  const int want = tc_hgroup(s) * (2 * s.T + 1);
+  return want < nheads ? want : nheads;
+}
+
 size_t tc_ctrl_bytes(const Shape& s) {
   return sizeof(uint32_t) * (tc::kCtrlDone + (size_t)s.E * s.H * 2 * s.T) + 256;
 }
@@ -974,21 +1007,11 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
       p->dtype == MA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int nheads = s.E * s.H;
   const int P = 2 * s.T;
-  // heads per wavefront phase slot: more heads in flight -> a longer distance
-  // between dependent items (a round is 2T * hgroup * 128 items)
   // tiles per (head, phase): 128 for b = 128, 32 for b = 64 (two items per tile)
   const int tiles = s.b * s.b / tc::kT;
-  // measured best on B200 for b = 128 (1: 856 us, 2: 785 us, 3: 808 us,
-  // 4: 803 us); the same round length (1024 tiles) for b = 64
-  int hgroup = 256 / tiles;
-  const char* hg = getenv("MA_TC_GROUP");
-  if (hg) hgroup = atoi(hg);
-  if (hgroup < 1) hgroup = 1;
-  if (hgroup > nheads) hgroup = nheads;
-  // The workspace holds the arrays of ws.tc_slots heads.  A slot is reused
-  // by head h + slots once head h's output phase is done, so a group of
-  // hgroup heads needs hgroup * (2T + 1) slots to keep dependencies pointing
-  // to earlier rounds of the wavefront: shrink the group to what exists.
+  int hgroup = tc_hgroup(s);
+  // The workspace holds the arrays of ws.tc_slots heads (tc_slots() for
+  // ma_fwd's layout): shrink the group to what exists.
   const int max_slots = ws.tc_slots > 0 && ws.tc_slots < nheads ? ws.tc_slots : nheads;
   if (hgroup * (2 * s.T + 1) > max_slots) hgroup = max_slots / (2 * s.T + 1) > 1 ? max_slots / (2 * s.T + 1) : 1;
   int slots = hgroup * (2 * s.T + 1);
@@ -1055,6 +1078,16 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   tp.cr = reinterpret_cast<float*>(w + ws.cr);
   tp.ctrl = reinterpret_cast<uint32_t*>(w + ws.ctrl);
   tp.status = p->status;
+  tp.status_host = p->status_host;
+  tp.stall_head = tp.stall_phase = -1;
+  const char* stall = getenv("MA_TEST_STALL_DEP");  // "head,phase" (tests only)
+  if (stall) {
+    int sh = -1, sp = -1;
+    if (sscanf(stall, "%d,%d", &sh, &sp) == 2 && sh >= 0 && sh < nheads && sp >= 1 && sp < P) {
+      tp.stall_head = sh;
+      tp.stall_phase = sp;
+    }
+  }
   tp.H = s.H;
   tp.nheads = nheads;
   tp.T = s.T;

@@ -93,6 +93,7 @@ struct Params {
   uint4* lsex;           // [head][j][l]: log-sum-exp of the L-step rows, as B_ext rows
   uint32_t* abort;
   uint32_t* status;
+  uint32_t* status_host;  // host mirror of the status word (optional)
   int H;
   int heads;             // E * H
   int first;             // R-step of round 0: A = q blocks, cr = 1
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 2) tc256_kernel(const __grid_constan
   const uint32_t A = (sbase + kSmallBytes + 1023u) & ~1023u;  // SW128 tiles
   const uint32_t B = A + kABytes;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const Guard guard{p.abort, p.status, p.timeout_ns};
+  const Guard guard{p.abort, p.status, p.timeout_ns, p.status_host};
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem_raw + kOffTmem);
   const float* vecB = reinterpret_cast<const float*>(smem_raw + kOffVecB);
   auto bar = [&](int off) { return sbase + kOffBar + off; };
@@ -716,6 +717,7 @@ cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
   if (ws.clx == 0 || ws.lsex == 0) return cudaErrorInvalidValue;  // layout without the rows
   prm.abort = reinterpret_cast<uint32_t*>(w + ws.ctrl) + 1;
   prm.status = p->status;
+  prm.status_host = p->status_host;
   prm.H = s.H;
   prm.heads = heads;
   prm.sm_scale = s.sm_scale;

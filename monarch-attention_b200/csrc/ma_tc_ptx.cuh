@@ -326,9 +326,16 @@ struct Guard {
   uint32_t* abort;
   uint32_t* status;
   unsigned long long limit;
+  uint32_t* status_host;  // page-locked host mirror of the status word, or null
   __device__ __forceinline__ void raise(uint32_t bit) const {
     atomicOr(status, bit);
     atomicExch(abort, 1u);
+    // a plain system-scope store (no atomics on host memory): the host only
+    // learns that a failure happened; the exact bits are in *status
+    if (status_host != nullptr) {
+      asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(status_host), "r"(bit) : "memory");
+      __threadfence_system();
+    }
   }
 };
 

@@ -72,11 +72,21 @@ class PadType(StrEnum):
 
 _status_lock = threading.Lock()
 _status_words: dict[int, Tensor] = {}
+_status_mirrors: dict[int, Tensor] = {}
+
+# bits of the device status word (include/ma_api.h)
+_STATUS_NAMES = {_lib.MA_STATUS_WAIT_TIMEOUT: "a bounded device wait ran out",
+                 _lib.MA_STATUS_TMEM_FAIL: "tensor-memory allocation failed",
+                 _lib.MA_STATUS_BAD_ITEM: "the scheduler produced an out-of-range item"}
+
+
+def _dev_index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
 
 
 def status_word(device: torch.device) -> Tensor:
     """Per-device int32 word into which kernels OR failure bits (MA_STATUS_*)."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+    idx = _dev_index(device)
     with _status_lock:
         w = _status_words.get(idx)
         if w is None:
@@ -85,14 +95,73 @@ def status_word(device: torch.device) -> Tensor:
         return w
 
 
+_mirror_refused: set[int] = set()
+
+
+def _status_mirror(device: torch.device) -> Tensor:
+    """Per-device page-locked host word a failing kernel also writes (the
+    ``status_host`` field of ma_fwd_params): the host learns of a failure
+    without reading device memory."""
+    idx = _dev_index(device)
+    with _status_lock:
+        h = _status_mirrors.get(idx)
+        if h is None:
+            h = torch.zeros(1, dtype=torch.int32).pin_memory()
+            _status_mirrors[idx] = h
+        return h
+
+
+def _mirror_ptr(device: torch.device) -> int:
+    """Address of the host mirror, or 0 where the library refused it (pinned
+    memory that is not mapped into the device's address space); failures are
+    then found by check_status() / check=True only."""
+    if _dev_index(device) in _mirror_refused:
+        return 0
+    return _status_mirror(device).data_ptr()
+
+
 def read_status(device: torch.device | None = None, reset: bool = True) -> int:
     """Synchronously read (and by default clear) the device status word."""
     device = device or torch.device("cuda", torch.cuda.current_device())
     w = status_word(device)
     val = int(w.item())
-    if reset and val:
-        w.zero_()
+    if reset:
+        if val:
+            w.zero_()
+        _status_mirror(device).zero_()
     return val
+
+
+def _raise_device_failure(device: torch.device, bits: int) -> None:
+    what = "; ".join(n for b, n in _STATUS_NAMES.items() if bits & b) or f"bits {bits:#x}"
+    raise _lib.MonarchAttentionError(
+        _lib.MA_ERR_DEVICE,
+        f"monarch attention: a kernel on {device} reported a device-side failure ({what}, "
+        f"status {bits:#x}); the output of that call is not valid")
+
+
+def check_status(device: torch.device | None = None) -> None:
+    """Wait for the device, then raise MonarchAttentionError (code
+    MA_ERR_DEVICE) if a kernel on it reported a failure since the last check;
+    the status is cleared either way."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    torch.cuda.synchronize(device)
+    bits = read_status(device)
+    if bits:
+        _raise_device_failure(device, bits)
+
+
+def _check_previous(device: torch.device) -> None:
+    """Lazy check at the start of every call: a failure of an earlier call on
+    this device shows in the host mirror (a host read, no synchronisation)."""
+    if _dev_index(device) in _mirror_refused:
+        return
+    h = _status_mirror(device)
+    if int(h[0]) != 0:
+        torch.cuda.synchronize(device)
+        bits = read_status(device) or int(h[0])
+        h.zero_()
+        _raise_device_failure(device, bits)
 
 
 def _impl_code(impl) -> int:
@@ -174,7 +243,7 @@ def _needs_grad(q: Tensor, k: Tensor, v: Tensor) -> bool:
 
 def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int,
                       B: int, pre_pad: bool, *, impl=None, scales: tuple | None = None,
-                      out: Tensor | None = None) -> Tensor:
+                      out: Tensor | None = None, check: bool = False) -> Tensor:
     """MonarchAttention forward on the current CUDA stream.
 
     Same arguments and result as ``monarch_attention_torch``
@@ -189,6 +258,12 @@ def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None,
     ``(E, N, H, Dv)`` buffer of the next projection seen through
     ``.permute(0, 2, 1, 3)``; with q, k, v passed as the same kind of views
     of the (E, N, H*D) projections, no layout copy is made on either side.
+
+    Device-side failures (a bounded wait in a kernel that ran out) raise
+    ``MonarchAttentionError`` with code MA_ERR_DEVICE: at the latest at the
+    next call on the same device (the kernel writes a page-locked host word,
+    so this costs no synchronisation), immediately with ``check=True`` (which
+    waits for the device), or from ``check_status()``.
     """
     _check_inputs(q, k, v)
     if _needs_grad(q, k, v):
@@ -196,9 +271,13 @@ def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None,
             raise RuntimeError("gradients through float8 e4m3 inputs are not supported")
         if out is not None:
             raise ValueError("out= cannot be used when gradients are required")
-        return training.MonarchAttentionFunction.apply(q, k, v, attn_mask, T, B, pre_pad, impl,
-                                                       _kernel_forward)
-    return _kernel_forward(q, k, v, attn_mask, T, B, pre_pad, impl, scales, out)
+        res = training.MonarchAttentionFunction.apply(q, k, v, attn_mask, T, B, pre_pad, impl,
+                                                      _kernel_forward)
+    else:
+        res = _kernel_forward(q, k, v, attn_mask, T, B, pre_pad, impl, scales, out)
+    if check:
+        check_status(q.device)
+    return res
 
 
 def _kernel_forward(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int, B: int,
@@ -220,6 +299,7 @@ def _kernel_forward(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T
         if out.device != q.device:
             raise ValueError("out is on a different device than the inputs")
     lib = _lib.load()
+    _check_previous(q.device)
     p, keep = build_params(q, k, v, out, attn_mask, T, B, pre_pad, _impl_code(impl), scales)
     nbytes = lib.ma_workspace_bytes(ctypes.byref(p))
     if nbytes == 0:
@@ -228,11 +308,17 @@ def _kernel_forward(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T
         ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
         p.workspace, p.workspace_bytes = ws.data_ptr(), nbytes
         p.status = status_word(q.device).data_ptr()
+        p.status_host = _mirror_ptr(q.device)
         stream = torch.cuda.current_stream(q.device).cuda_stream
         nvtx = os.environ.get("MA_NVTX") == "1"
         if nvtx:
             torch.cuda.nvtx.range_push(f"monarch_attention E{E} H{H} N{N} B{B} T{T}")
         rc = lib.ma_fwd(ctypes.byref(p), ctypes.c_void_p(stream))
+        if rc == _lib.MA_ERR_BAD_PARAMS and p.status_host and \
+                b"status_host" in lib.ma_last_error_detail():
+            _mirror_refused.add(_dev_index(q.device))
+            p.status_host = None
+            rc = lib.ma_fwd(ctypes.byref(p), ctypes.c_void_p(stream))
         if nvtx:
             torch.cuda.nvtx.range_pop()
     _lib.check(rc)

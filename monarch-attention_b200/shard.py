@@ -30,6 +30,36 @@ def shard_range(E: int, H: int, world: int, rank: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
+def shard_problem(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask, scales,
+                  world: int, rank: int):
+    """This rank's heads of an (E, H) problem as a smaller (E', H') problem.
+
+    Returns ``(q, k, v, mask, scales, (start, stop))`` with contiguous copies.
+    When E is a multiple of ``world`` the shard is whole batch rows
+    (E / world, H) with their mask rows; otherwise it is laid out as
+    (stop - start, 1) heads, each with the mask row of its batch row, so any
+    shard runs through the same operator unchanged.  ``scales`` (e4m3
+    per-(e, h) factors, each (E, H)) follow the heads.
+    """
+    E, H = q.shape[:2]
+    a, b = shard_range(E, H, world, rank)
+    if world == 1:
+        return q, k, v, mask, scales, (a, b)
+    if E % world == 0:
+        e0, e1 = a // H, b // H
+        sl = lambda t: t[e0:e1].contiguous()
+        return (sl(q), sl(k), sl(v), None if mask is None else sl(mask),
+                None if scales is None else tuple(sl(s) for s in scales), (a, b))
+    n = b - a
+    fl = lambda t: t.reshape(E * H, *t.shape[2:])[a:b].unsqueeze(1).contiguous()
+    m = None
+    if mask is not None:
+        m = mask[torch.arange(a, b, device=mask.device) // H].contiguous()
+    sc = None if scales is None else tuple(s.reshape(E * H)[a:b].reshape(n, 1).contiguous()
+                                           for s in scales)
+    return fl(q), fl(k), fl(v), m, sc, (a, b)
+
+
 def take_shard(x: torch.Tensor, start: int, stop: int) -> torch.Tensor:
     """Rows [start, stop) of the flattened (E*H) leading dims of x, as (1, n, ...)."""
     E, H = x.shape[:2]
@@ -54,10 +84,11 @@ def max_over_ranks(value: float, device=None) -> float:
 
 
 def gather_shards(shard: torch.Tensor, E: int, H: int) -> torch.Tensor:
-    """All-gather per-rank (1, n_r, N, D) shards into the full (E, H, N, D) output."""
+    """All-gather per-rank (E', H', N, D) output shards (E' * H' = the rank's
+    head count) into the full (E, H, N, D) output on every rank."""
     world = dist.get_world_size()
     sizes = [shard_range(E, H, world, r) for r in range(world)]
-    flat = shard.reshape(shard.shape[1], *shard.shape[2:])
+    flat = shard.reshape(shard.shape[0] * shard.shape[1], *shard.shape[2:])
     maxn = max(b - a for a, b in sizes)
     pad = torch.zeros((maxn, *flat.shape[1:]), dtype=flat.dtype, device=flat.device)
     pad[: flat.shape[0]] = flat

@@ -28,7 +28,7 @@ def test_library_exports_every_declared_symbol():
     lib = mab.load_library()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.ma_api_version() == 1
+    assert lib.ma_api_version() == 2
 
 
 def good_params(**over):
@@ -117,3 +117,34 @@ def test_noalloc_entry_rejects_on_the_host():
     assert b"tcgen05" in lib.ma_last_error_detail()
     p = good_params(E=0)
     assert fn(ctypes.byref(p), None) == 2
+
+
+def tc_params(E=4, H=16, N=16384, b=128, T=2, D=128):
+    p = good_params(E=E, H=H, N=N, D=D, Dv=D, block_size=b, num_steps=T)
+    strides = (H * N * D, N * D, D, 1)
+    for name in ("q_stride", "k_stride", "v_stride", "o_stride"):
+        arr = getattr(p, name)
+        for i, s in enumerate(strides):
+            arr[i] = s
+    return p
+
+
+@pytest.mark.parametrize("E,H,N,b,T", [(4, 16, 16384, 128, 2), (4, 16, 4096, 64, 2),
+                                       (1, 3, 16384, 128, 3)])
+def test_tc_workspace_holds_only_the_cycled_slots(E, H, N, b, T):
+    """The persistent tcgen05 kernel cycles through at most 2 x (2T+1) head
+    slots of al / y / ar / cl / cr (hgroup heads per wavefront phase: 2 at
+    b = 128, 8 at b = 64 -> capped by the head count), not all E*H heads."""
+    lib = mab.load_library()
+    p = tc_params(E, H, N, b, T)
+    assert lib.ma_select_impl(ctypes.byref(p)) == _lib.IMPL_TC
+    n = lib.ma_workspace_bytes(ctypes.byref(p))
+    M = N // b
+    per_head = b * M * (128 * 3 * 2 + 4 + 4 + 16)
+    hgroup = 2 if b == 128 else 8
+    slots = min(E * H, hgroup * (2 * T + 1))
+    ctrl = 4 * (64 + E * H * 2 * T) + 4096
+    assert n <= slots * per_head + ctrl
+    assert n >= slots * b * M * 128 * 3 * 2
+    if b == 128 and E * H > slots:
+        assert n < E * H * per_head / 3  # ~0.85 GB before, ~125 MB now

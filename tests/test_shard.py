@@ -72,3 +72,43 @@ def test_two_rank_gather_matches_single_process(tmp_path):
     err, t = map(float, open(path).read().split())
     assert err < 1e-6
     assert t == float(world)
+
+
+def _problem_worker(rank, world, port, result_path):
+    """shard_problem + gather_shards exactly as bench.py uses them, with the
+    oracle standing in for the kernel: each shard is run as its own (E', H')
+    problem with its own mask rows."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from oracle.ma_oracle import monarch_attention_oracle
+        from monarch_attention_b200.shard import shard_problem
+        g = torch.Generator().manual_seed(9)
+        E, H, N, D, B, T = 2, 3, 40, 8, 8, 2
+        q, k, v = (torch.randn(E, H, N, D, generator=g) for _ in range(3))
+        mask = torch.ones(E, N, dtype=torch.bool)
+        mask[1, 17:] = False
+        scales = tuple(torch.rand(E, H, generator=g) for _ in range(3))
+        qs, ks, vs, ms, ss, (a, b) = shard_problem(q, k, v, mask, scales, world, rank)
+        assert qs.shape[0] * qs.shape[1] == b - a and qs.is_contiguous()
+        # the scales follow the heads
+        assert torch.equal(ss[0].reshape(-1), scales[0].reshape(-1)[a:b])
+        o = monarch_attention_oracle(qs.numpy(), ks.numpy(), vs.numpy(), ms.numpy(), T, B, False)
+        full = gather_shards(torch.from_numpy(o), E, H)
+        if rank == 0:
+            ref = monarch_attention_oracle(q.numpy(), k.numpy(), v.numpy(), mask.numpy(),
+                                           T, B, False)
+            with open(result_path, "w") as f:
+                f.write(f"{float(np.abs(full.numpy() - ref).max())}")
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_shard_problem_gather_matches_single_process(world, tmp_path):
+    """world 2 splits whole batch rows; world 3 splits inside a batch row
+    (the (n, 1) layout with per-head mask rows)."""
+    path = str(tmp_path / "res.txt")
+    mp.spawn(_problem_worker, args=(world, _free_port(), path), nprocs=world, join=True)
+    assert float(open(path).read()) < 1e-6
