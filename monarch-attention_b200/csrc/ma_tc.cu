@@ -29,7 +29,7 @@
 //   warp 12          scheduler + TMA producer (3-entry ring, 2 tiles each)
 //   warp 13          TMEM allocator + GEMM1 issuer
 //   warps 14, 15     TMA stores + publication of alternate items
-// The softmax and the epilogue stream each row out of TMEM in 16-column
+// The softmax and the epilogue stream each row out of TMEM in 32-column
 // chunks, the next chunk's load in flight while the current one is
 // processed, in small loop bodies with few live registers (the whole CTA
 // gets 128 registers per thread).
@@ -180,31 +180,32 @@ __device__ __forceinline__ void trace_stamp(const TcParams& p, uint32_t n, int s
 // 128 TMEM accumulator columns of this lane -> scaled 16-bit row of an output
 // tile staged in SMEM in the SW128 layout the TMA store expects: row r of
 // half h at h*16K + r*128, 16-byte unit c at position c ^ (r & 7).  The row
-// is read in 16-column chunks with the next chunk's load in flight.
+// is read in 32-column chunks with the next chunk's load in flight.
 template <bool BF16>
 __device__ __forceinline__ void stage_row128(uint32_t tile, int row, uint32_t taddr, float scale) {
-  uint32_t ca[16], cb[16];
+  uint32_t ca[32], cb[32];
   const uint32_t rbase = tile + row * 128;
   const uint64_t sc2 = f2pack(scale, scale);
-  auto put = [&](const uint32_t(&cv)[16], int ch) {
+  // chunk ch (32 columns) = 16-byte units u = 4 ch .. 4 ch + 3
+  auto put = [&](const uint32_t(&cv)[32], int ch) {
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
+    for (int t = 0; t < 4; ++t) {
       uint32_t w[4];
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         w[q] = scale_pack2<BF16>(cv[8 * t + 2 * q], cv[8 * t + 2 * q + 1], sc2);
-      const int u = 2 * ch + t;
+      const int u = 4 * ch + t;
       st_shared_v4(rbase + (u >> 3) * kHalf + (((u & 7) ^ (row & 7)) << 4), w[0], w[1], w[2], w[3]);
     }
   };
-  tmem_ld16(taddr, ca);
+  tmem_ld32(taddr, ca);
   tmem_wait_ld();
 #pragma unroll 1
-  for (int ch = 0; ch < 8; ch += 2) {
-    tmem_ld16(taddr + 16 * (ch + 1), cb);
+  for (int ch = 0; ch < 4; ch += 2) {
+    tmem_ld32(taddr + 32 * (ch + 1), cb);
     put(ca, ch);
     tmem_wait_ld();
-    if (ch + 2 < 8) tmem_ld16(taddr + 16 * (ch + 2), ca);
+    if (ch + 2 < 4) tmem_ld32(taddr + 32 * (ch + 2), ca);
     put(cb, ch + 1);
     tmem_wait_ld();
   }
@@ -561,30 +562,31 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
                      row * 128);
       }
 
-      // The row of S (128 fp32) is streamed out of TMEM in 16-column chunks,
+      // The row of S (128 fp32) is streamed out of TMEM in 32-column chunks,
       // the next chunk's load in flight while the current one is processed
-      // (small loop bodies, few live registers): pass 1 takes the row
-      // maximum, pass 2 exponentiates and sums (P goes back to TMEM; for L
-      // items e goes back in place), pass 3 (L only) normalises and writes
-      // P^T to shared memory.  Chunks c_lo .. c_hi - 1 (an even count) are
-      // this row's columns 16 c ..
-      const int c_lo = 4 * h_lo, c_hi = 4 * h_hi;
+      // (a chunk's 32 exponentials take longer than a TMEM load, so the load
+      // latency is hidden): pass 1 takes the row maximum, pass 2
+      // exponentiates and sums (P goes back to TMEM; for L items e goes back
+      // in place), pass 3 (L only) normalises and writes P^T to shared
+      // memory.  Chunks c_lo .. c_hi - 1 (an even count) are this row's
+      // columns 32 c ..
+      const int c_lo = 2 * h_lo, c_hi = 2 * h_hi;
       const bool rk = kind == KIND_R;
       float c = 1.0f;  // R: sm_scale / (cr_j + eps)
       if (rk) c = p.sm_scale / ((ph > 0 ? vec[row] : 1.0f) + kEps);
-      uint32_t ca[16], cb[16];
+      uint32_t ca[32], cb[32];
       float mx;
       {
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         // (L / output items: S already holds x = S - cl[k], from GEMM1)
-        auto max_chunk = [&](const uint32_t(&cv)[16]) {
+        auto max_chunk = [&](const uint32_t(&cv)[32]) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(cv[i]));
+          for (int i = 0; i < 32; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], __uint_as_float(cv[i]));
         };
 #pragma unroll 1
         for (int ch = c_lo; ch < c_hi; ch += 2) {  // the maximum needs no prefetch
-          tmem_ld16(tS + 16 * ch, ca);
-          tmem_ld16(tS + 16 * (ch + 1), cb);
+          tmem_ld32(tS + 32 * ch, ca);
+          tmem_ld32(tS + 32 * (ch + 1), cb);
           tmem_wait_ld();
           max_chunk(ca);
           max_chunk(cb);
@@ -607,11 +609,11 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       const uint64_t ua2 = f2pack(u_a, u_a), ub2 = f2pack(u_b, u_b);
       {
         // e of chunk ch; back to TMEM as fp32 in place (L) or as packed
-        // 16-bit pairs into columns 8 ch .. 8 ch + 7 (R / out: those S
+        // 16-bit pairs into columns 16 ch .. 16 ch + 15 (R / out: those S
         // columns were read already, and the chunk in flight lies beyond)
-        auto exp_chunk = [&](uint32_t(&cv)[16], int ch) {
+        auto exp_chunk = [&](uint32_t(&cv)[32], int ch) {
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
+          for (int t = 0; t < 16; ++t) {
             const uint64_t x2 = f2pack(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1]));
             const uint64_t u2 = ffma2(x2, ua2, ub2);
             float u0, u1;
@@ -624,23 +626,23 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
             cv[2 * t + 1] = __float_as_uint(e1);
           }
           if (kind == KIND_L) {
-            tmem_st16(tS + 16 * ch, cv);
+            tmem_st32(tS + 32 * ch, cv);
           } else {
-            uint32_t pk[8];
+            uint32_t pk[16];
 #pragma unroll
-            for (int t = 0; t < 8; ++t)
+            for (int t = 0; t < 16; ++t)
               pk[t] = pack2<BF16>(__uint_as_float(cv[2 * t]), __uint_as_float(cv[2 * t + 1]));
-            tmem_st8(tS + 8 * ch, pk);
+            tmem_st16(tS + 16 * ch, pk);
           }
         };
-        tmem_ld16(tS + 16 * c_lo, ca);
+        tmem_ld32(tS + 32 * c_lo, ca);
         tmem_wait_ld();
 #pragma unroll 1
         for (int ch = c_lo; ch < c_hi; ch += 2) {
-          tmem_ld16(tS + 16 * (ch + 1), cb);
+          tmem_ld32(tS + 32 * (ch + 1), cb);
           exp_chunk(ca, ch);
           tmem_wait_ld();
-          if (ch + 2 < c_hi) tmem_ld16(tS + 16 * (ch + 2), ca);
+          if (ch + 2 < c_hi) tmem_ld32(tS + 32 * (ch + 2), ca);
           exp_chunk(cb, ch + 1);
           tmem_wait_ld();
         }
@@ -687,30 +689,30 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           for (int cc = 0; cc < 8; ++cc)
             st_shared_v4(prow + (1 - pk_row) * kHalf + ((cc ^ (row & 7)) << 4), 0u, 0u, 0u, 0u);
         }
-        // chunk ch = two 16-byte units (8 columns each) of the row: unit
-        // u = 2 ch + t of the 128-column row sits in half u / 8, position
+        // chunk ch = four 16-byte units (8 columns each) of the row: unit
+        // u = 4 ch + t of the 128-column row sits in half u / 8, position
         // (u % 8) ^ (row % 8)
         const uint64_t so2 = f2pack(scale_out, scale_out);
-        auto st_chunk = [&](const uint32_t(&cv)[16], int ch) {
+        auto st_chunk = [&](const uint32_t(&cv)[32], int ch) {
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
+          for (int t = 0; t < 4; ++t) {
             uint32_t a[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               a[q] = scale_pack2<BF16>(cv[8 * t + 2 * q], cv[8 * t + 2 * q + 1], so2);
-            const int u = 2 * ch + t;
+            const int u = 4 * ch + t;
             st_shared_v4(prow + (u >> 3) * kHalf + (((u & 7) ^ (row & 7)) << 4), a[0], a[1], a[2],
                          a[3]);
           }
         };
-        tmem_ld16(tS + 16 * c_lo, ca);
+        tmem_ld32(tS + 32 * c_lo, ca);
         tmem_wait_ld();
 #pragma unroll 1
         for (int ch = c_lo; ch < c_hi; ch += 2) {
-          tmem_ld16(tS + 16 * (ch + 1), cb);
+          tmem_ld32(tS + 32 * (ch + 1), cb);
           st_chunk(ca, ch);
           tmem_wait_ld();
-          if (ch + 2 < c_hi) tmem_ld16(tS + 16 * (ch + 2), ca);
+          if (ch + 2 < c_hi) tmem_ld32(tS + 32 * (ch + 2), ca);
           st_chunk(cb, ch + 1);
           tmem_wait_ld();
         }
