@@ -60,6 +60,13 @@ CONFIGS = {
         Config("long4k_bf16", 4, 16, 4096, 128, 64, 2, "bf16", scaled=False, seed=1004),
         Config("long16k_bf16", 4, 16, 16384, 128, 128, 2, "bf16", scaled=False, seed=1004),
         Config("long64k_bf16", 4, 16, 65536, 128, 256, 2, "bf16", scaled=False, seed=1004),
+        # BART-base encoder layers at the lengths bart/benchmark.py:42 evaluates
+        # (batch 4, 12 heads of 64, (b, T) per length), with a float key-padding
+        # mask (bart/model.py:145-152): valid length uniform in [N/2, N]
+        Config("bart1k_bf16", 4, 12, 1024, 64, 32, 3, "bf16", mask_min_len=512, seed=1006),
+        Config("bart2k_bf16", 4, 12, 2048, 64, 32, 2, "bf16", mask_min_len=1024, seed=1007),
+        Config("bart4k_bf16", 4, 12, 4096, 64, 64, 2, "bf16", mask_min_len=2048, seed=1008),
+        Config("bart8k_bf16", 4, 12, 8192, 64, 64, 2, "bf16", mask_min_len=4096, seed=1009),
         Config("long4k_e4m3", 4, 16, 4096, 128, 64, 2, "e4m3", scaled=False, seed=1004),
         Config("long16k_e4m3", 4, 16, 16384, 128, 128, 2, "e4m3", scaled=False, seed=1004),
         Config("long64k_e4m3", 4, 16, 65536, 128, 256, 2, "e4m3", scaled=False, seed=1004),

@@ -33,6 +33,7 @@ cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
 bool tc_supports(const ma_fwd_params* p, const Shape& s);
 int tc_slots(const Shape& s);
 size_t tc_ctrl_bytes(const Shape& s);
+size_t tc_valid_bytes(const ma_fwd_params* p, const Shape& s);
 cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, cudaStream_t st,
                    int* nlaunch);
 }  // namespace ma
@@ -90,15 +91,16 @@ Shape make_shape(const ma_fwd_params* p) {
 
 // Workspace layout for the kernel family `impl` (MA_IMPL_*).  conv: reserve
 // bf16 copies of e4m3 q / k / v (tensor-core kernels).  The persistent
-// tcgen05 kernel (b = 64, 128) cycles through tc_slots() head slots of the
-// al / y / ar / cl / cr arrays and needs no lmax / lsum; every other kernel
-// keeps the arrays of all E * H heads.
-WsLayout make_layout(const Shape& s, int dtype, bool conv, int impl) {
+// tcgen05 kernel (b != 256) cycles through tc_slots() head slots of the
+// al / y / ar / cl / cr arrays, needs no lmax / lsum, and takes a token
+// validity bitmap of valid_bytes when masked; every other kernel keeps the
+// arrays of all E * H heads.
+WsLayout make_layout(const Shape& s, int dtype, bool conv, int impl, size_t valid_bytes) {
   WsLayout w{};
   // intermediates are kept in the input precision; e4m3 inputs use bf16
   w.store_bytes = dtype == MA_DTYPE_F32 ? 4 : 2;
-  const bool tc_shape = s.D == 128 && s.b == s.M && (s.b == 64 || s.b == 128 || s.b == 256);
-  const bool persistent = impl == MA_IMPL_TC && tc_shape && s.b != 256;
+  const bool tc = impl == MA_IMPL_TC;
+  const bool persistent = tc && s.b != 256;
   const size_t heads = persistent ? (size_t)tc_slots(s) : (size_t)s.E * s.H;
   const size_t bm = (size_t)s.b * s.M;
   size_t off = 0;
@@ -107,11 +109,14 @@ WsLayout make_layout(const Shape& s, int dtype, bool conv, int impl) {
   w.ar = off; off = align_up(off + heads * bm * s.D * w.store_bytes, 256);
   w.cl = off; off = align_up(off + heads * bm * 4, 256);
   w.cr = off; off = align_up(off + heads * bm * 4, 256);
-  if (tc_shape) {
+  if (tc) {
     w.clx = off; off = align_up(off + heads * bm * 16, 256);
     if (s.b == 256) {
       w.lsex = off; off = align_up(off + heads * bm * 16, 256);
     }
+  }
+  if (persistent && valid_bytes > 0) {
+    w.valid = off; off = align_up(off + valid_bytes, 256);
   }
   const size_t lrows = persistent ? 0 : heads * bm;
   w.lmax = off; off = align_up(off + lrows * 4, 256);
@@ -265,7 +270,7 @@ size_t ma_workspace_bytes(const ma_fwd_params* p) {
   g_detail = keep;
   if (rc != MA_OK) return 0;
   const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
-  return make_layout(s, p->dtype, conv, impl).total;
+  return make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s)).total;
 }
 
 int ma_select_impl(const ma_fwd_params* p) {
@@ -287,7 +292,7 @@ int ma_fwd(const ma_fwd_params* p, void* stream) {
   rc = select_impl(p, s, &impl);
   if (rc != MA_OK) return rc;
   const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
-  const WsLayout ws = make_layout(s, p->dtype, conv, impl);
+  const WsLayout ws = make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s));
   if (p->workspace == nullptr || p->workspace_bytes < ws.total)
     return fail(MA_ERR_WORKSPACE, "workspace needs " + std::to_string(ws.total) + " bytes, got " +
                                       std::to_string(p->workspace_bytes));

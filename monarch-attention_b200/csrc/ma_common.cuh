@@ -41,6 +41,8 @@ struct Shape {
 //   lsex [b][M] x 16 bytes          -- the b = 256 kernel's L-step
 //                                      log-sum-exp in the same form
 //   lmax, lsum [b][M] fp32          -- L-step softmax statistics (generic path)
+//   valid [E][N / 32] u32           -- token validity bitmap of a masked call
+//                                      (tcgen05 kernel; 0 = not used)
 //   ctrl                            -- dependency counters (tcgen05 path)
 //   xq, xk, xv                      -- bf16 copies of e4m3 q / k / v for the
 //                                      tensor-core kernels (0 = not used)
@@ -49,7 +51,7 @@ struct Shape {
 //                                      slot limit; every head in ma_fwd's
 //                                      workspace, fewer in compact ones)
 struct WsLayout {
-  size_t al, y, ar, cl, cr, clx, lsex, lmax, lsum, ctrl, ctrl_bytes, total;
+  size_t al, y, ar, cl, cr, clx, lsex, lmax, lsum, valid, ctrl, ctrl_bytes, total;
   size_t xq, xk, xv;
   int tc_slots;
   int store_bytes;  // bytes per element of al / y / ar

@@ -125,8 +125,13 @@ extern "C" int ma_fwd_noalloc(const ma_fwd_params* p, void* stream) {
     return MA_ERR_NULL_POINTER;
   }
   const ma::Shape s = shape_of(p);
-  if (!ma::tc_supports(p, s)) {  // the b = 256 kernel needs every head's arrays
-    ma::set_error_detail("ma_fwd_noalloc runs the persistent tcgen05 kernel only (block size 64 or 128)");
+  // the b = 256 kernel needs every head's arrays; masked calls need a bitmap
+  // the static array does not hold
+  if (!ma::tc_supports(p, s) || s.D != 128 || s.b != s.M || (s.b != 64 && s.b != 128) ||
+      p->mask_dtype != MA_MASK_NONE) {
+    ma::set_error_detail(
+        "ma_fwd_noalloc runs the persistent tcgen05 kernel only (block size = number of "
+        "blocks = 64 or 128, head dim 128, bf16/fp16, no mask); use ma_fwd for this shape");
     return MA_ERR_UNSUPPORTED;
   }
   const int nheads = s.E * s.H;

@@ -1,0 +1,13 @@
+// Persistent tcgen05 kernel (ma_tc_kernel.cuh) compiled for block size
+// b = 32, 64 blocks, head dim 64 (one translation unit per shape, so the
+// shapes build in parallel).
+#include "ma_tc_kernel.cuh"
+
+namespace ma {
+namespace tc {
+template cudaError_t launch_tc<true, 32, 64, 64, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<true, 32, 64, 64, true>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 32, 64, 64, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 32, 64, 64, true>(const TcParams&, int, cudaStream_t);
+}  // namespace tc
+}  // namespace ma

@@ -109,7 +109,8 @@ def test_config_small(name, impl, cuda_device):
 # full-size configs: every head computed, a sample of heads checked exactly
 # ---------------------------------------------------------------------------
 FULL = ["cfg0_f32", "vit_bf16", "vit_n197_f16", "roberta_bf16", "dit_bf16", "long4k_bf16",
-        "long16k_bf16", "long64k_bf16"]
+        "long16k_bf16", "long64k_bf16", "bart1k_bf16", "bart2k_bf16", "bart4k_bf16",
+        "bart8k_bf16"]
 
 
 @pytest.mark.parametrize("name", FULL)
@@ -213,17 +214,57 @@ def test_block256_kernel_variants(T, dtype, views, cuda_device):
 
 
 # Shapes the reference accepts that the tensor-core kernels do not take (fp32,
-# a mask, Dv != D, ragged N with front padding, D != 128): the automatic
-# choice must fall back to a kernel that gets them right.
+# Dv != D, ragged N with front padding): the automatic choice must fall back
+# to a kernel that gets them right.
 FALLBACK = [
     ("f32_b64", dict(E=1, H=1, N=4096, D=128, B=64, T=2, dtype="f32", scaled=False), None),
-    ("mask_b128", dict(E=1, H=1, N=16384, D=128, B=128, T=2, dtype="bf16", scaled=False,
-                       mask_min_len=9000), None),
     ("dv64_b64", dict(E=1, H=1, N=4096, D=128, B=64, T=2, dtype="bf16", scaled=False, Dv=64), None),
     ("ragged_prepad_b64", dict(E=1, H=2, N=4000, D=128, B=64, T=2, dtype="bf16", scaled=False,
                                pre_pad=True), None),
-    ("d64_b64", dict(E=1, H=1, N=4096, D=64, B=64, T=2, dtype="f16"), None),
 ]
+
+
+# The persistent tcgen05 kernel's other shapes: head dim 64, b != M (tiles
+# packing 4 R items of b = 32, or 2 of b = 64 next to 1 L item of M = 128),
+# and key-padding masks (BART, bart/model.py:145-152: a float (E, N) mask).
+# Batch row 1 of the masked cases is fully masked, batch row 0 partly.
+TC_SHAPES = [
+    ("mask_b128", dict(N=16384, D=128, B=128, T=2, dtype="bf16", scaled=False), "part+full"),
+    ("mask_b64_d128", dict(N=4096, D=128, B=64, T=2, dtype="bf16", scaled=False), "part+full"),
+    ("d64_b64_f16", dict(N=4096, D=64, B=64, T=2, dtype="f16"), None),
+    ("d64_b128", dict(N=16384, D=64, B=128, T=2, dtype="bf16"), None),
+    ("bart2k_b32_m64", dict(N=2048, D=64, B=32, T=2, dtype="bf16"), "part+full"),
+    ("bart2k_b32_m64_t3", dict(N=2048, D=64, B=32, T=3, dtype="bf16"), "part"),
+    ("bart4k_b64", dict(N=4096, D=64, B=64, T=2, dtype="bf16"), "part+full"),
+    ("bart8k_b64_m128", dict(N=8192, D=64, B=64, T=2, dtype="bf16"), "part+full"),
+    ("bart8k_b64_m128_f16", dict(N=8192, D=64, B=64, T=2, dtype="f16"), "part"),
+]
+
+
+@pytest.mark.parametrize("name,shape,masking", TC_SHAPES, ids=[c[0] for c in TC_SHAPES])
+def test_tc_kernel_shapes_and_masks(name, shape, masking, cuda_device):
+    cfg = CONFIGS["long4k_bf16"].with_(E=2, H=1, **shape)
+    q, k, v, _m, _s = make_inputs(cfg, device="cpu")
+    mask = None
+    if masking is not None:
+        g = torch.Generator(device="cpu").manual_seed(17)
+        mask = torch.ones(cfg.E, cfg.N, dtype=torch.float32)  # float, as the BART hook passes
+        n_valid = int(torch.randint(cfg.N // 4, cfg.N - 1, (1,), generator=g))
+        mask[0, n_valid:] = 0.0
+        mask[0, torch.randint(0, n_valid, (cfg.N // 16,), generator=g)] = 0.0  # holes
+        if masking == "part+full":
+            mask[1] = 0.0
+    dq, dk, dv = (t.to(cuda_device) for t in (q, k, v))
+    dm = None if mask is None else mask.to(cuda_device)
+    assert mab.selected_impl(dq, dk, dv, dm, cfg.T, cfg.B, cfg.pre_pad) == "tc"
+    out = monarch_attention(dq, dk, dv, dm, cfg.T, cfg.B, cfg.pre_pad)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    ref = oracle_for(q, k, v, mask, cfg, "f32")
+    err = np.abs(got - ref).max()
+    assert err <= tol_for(cfg.dtype, ref), f"{name}: max|err|={err:.3g}"
 
 
 @pytest.mark.parametrize("name,shape,_", FALLBACK, ids=[c[0] for c in FALLBACK])
