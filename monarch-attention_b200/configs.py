@@ -57,6 +57,9 @@ CONFIGS = {
         Config("vit_n197_f16", 64, 12, 197, 64, 14, 2, "f16", pre_pad=True, seed=1005),
         Config("roberta_bf16", 32, 12, 512, 64, 32, 2, "bf16", mask_min_len=128, seed=1002),
         Config("dit_bf16", 32, 16, 1024, 72, 32, 3, "bf16", seed=1003),
+        # the DiT pipeline's default precision (dit/pipeline.py:147-159 loads
+        # the model without a dtype): fp32 inputs, fused FFMA kernel
+        Config("dit_f32", 32, 16, 1024, 72, 32, 3, "f32", seed=1003),
         Config("long4k_bf16", 4, 16, 4096, 128, 64, 2, "bf16", scaled=False, seed=1004),
         Config("long16k_bf16", 4, 16, 16384, 128, 128, 2, "bf16", scaled=False, seed=1004),
         Config("long64k_bf16", 4, 16, 65536, 128, 256, 2, "bf16", scaled=False, seed=1004),

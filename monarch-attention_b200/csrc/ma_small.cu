@@ -590,7 +590,13 @@ static cudaError_t launch(const SmallParams& sp, cudaStream_t st) {
 
 }  // namespace small
 
+// ma_small_f32.cu: the same fused kernel in fp32 (FFMA)
+bool small_f32_supports(const ma_fwd_params* p, const Shape& s);
+cudaError_t run_small_f32(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
+                          cudaStream_t st, int* nlaunch);
+
 bool small_supports(const ma_fwd_params* p, const Shape& s) {
+  if (p->dtype == MA_DTYPE_F32) return small_f32_supports(p, s);
   if (p->dtype != MA_DTYPE_BF16 && p->dtype != MA_DTYPE_F16) return false;
   if (s.b > small::kRows || s.M > small::kRows) return false;
   if (s.D != s.Dv || s.D % 8 != 0 || s.D > 128) return false;
@@ -611,6 +617,7 @@ bool small_supports(const ma_fwd_params* p, const Shape& s) {
 
 cudaError_t run_small(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
                       cudaStream_t st, int* nlaunch) {
+  if (p->dtype == MA_DTYPE_F32) return run_small_f32(p, s, ws, st, nlaunch);
   small::SmallParams sp{};
   sp.q = p->q; sp.k = p->k; sp.v = p->v; sp.out = p->out;
   for (int i = 0; i < 4; ++i) {

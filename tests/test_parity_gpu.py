@@ -49,9 +49,8 @@ def test_golden(path, impl, cuda_device):
     c = load_case(path)
     m = c["meta"]
     dt = m["dtype"]
-    if impl == "small" and not (dt in ("bf16", "f16") and m["B"] <= 32
-                                and -(-m["N"] // m["B"]) <= 32 and m["D"] == m["Dv"]
-                                and m["D"] % 8 == 0):
+    if impl == "small" and not (m["B"] <= 32 and -(-m["N"] // m["B"]) <= 32
+                                and m["D"] == m["Dv"] and m["D"] % 8 == 0):
         pytest.skip("outside the small-block kernel's shapes")
     q, k, v = (to_dev(c[n], dt, cuda_device) for n in ("q", "k", "v"))
     mask = None if "mask" not in c else torch.from_numpy(c["mask"]).to(cuda_device)
@@ -75,6 +74,7 @@ SMALL = {
     "vit_n197_f16": dict(E=2, H=2),
     "roberta_bf16": dict(E=3, H=2),
     "dit_bf16": dict(E=1, H=2),
+    "dit_f32": dict(E=1, H=2),
     "long4k_bf16": dict(E=1, H=2),
     "long16k_bf16": dict(E=1, H=1),
     "long64k_bf16": dict(E=1, H=1),
@@ -91,7 +91,7 @@ def oracle_for(q, k, v, mask, cfg, dt):
 @pytest.mark.parametrize("name", list(SMALL))
 def test_config_small(name, impl, cuda_device):
     cfg = CONFIGS[name].with_(**SMALL[name])
-    if impl == "small" and (cfg.dtype == "f32" or cfg.B > 32 or cfg.M > 32):
+    if impl == "small" and (cfg.B > 32 or cfg.M > 32):
         pytest.skip("outside the small-block kernel's shapes")
     q, k, v, mask, _ = make_inputs(cfg, device="cpu")
     out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
@@ -108,7 +108,7 @@ def test_config_small(name, impl, cuda_device):
 # ---------------------------------------------------------------------------
 # full-size configs: every head computed, a sample of heads checked exactly
 # ---------------------------------------------------------------------------
-FULL = ["cfg0_f32", "vit_bf16", "vit_n197_f16", "roberta_bf16", "dit_bf16", "long4k_bf16",
+FULL = ["cfg0_f32", "dit_f32", "vit_bf16", "vit_n197_f16", "roberta_bf16", "dit_bf16", "long4k_bf16",
         "long16k_bf16", "long64k_bf16", "bart1k_bf16", "bart2k_bf16", "bart4k_bf16",
         "bart8k_bf16"]
 
@@ -173,12 +173,14 @@ def test_caller_layout_in_and_out(impl, shape, cuda_device):
     assert torch.equal(o_buf.view(E, N, H, D).permute(0, 2, 1, 3), ref)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
 @pytest.mark.parametrize("csize", ["1", "2", "4"])
-def test_small_kernel_cluster_sizes(csize, cuda_device, monkeypatch):
-    """The small-block kernel splits a head over a cluster of 1, 2 or 4 CTAs;
-    every split gives the oracle's result (masked RoBERTa shape, T = 3)."""
+def test_small_kernel_cluster_sizes(csize, dtype, cuda_device, monkeypatch):
+    """The small-block kernels (mma.sync 16-bit, FFMA fp32) split a head over a
+    cluster of 1, 2 or 4 CTAs; every split gives the oracle's result (masked
+    RoBERTa shape, T = 3)."""
     monkeypatch.setenv("MA_SMALL_CLUSTER", csize)
-    cfg = CONFIGS["roberta_bf16"].with_(E=2, H=2, T=3)
+    cfg = CONFIGS["roberta_bf16"].with_(E=2, H=2, T=3, dtype=dtype)
     q, k, v, mask, _ = make_inputs(cfg, device="cpu")
     out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
                             mask.to(cuda_device), cfg.T, cfg.B, cfg.pre_pad, impl="small")
@@ -269,6 +271,8 @@ def test_tc_kernel_shapes_and_masks(name, shape, masking, cuda_device):
 
 @pytest.mark.parametrize("name,shape,_", FALLBACK, ids=[c[0] for c in FALLBACK])
 def test_shapes_outside_the_tensor_core_kernels(name, shape, _, cuda_device):
+    """(f32 b = 64 has M = 64 > 32: neither fused kernel takes it; the
+    generic kernels do.)"""
     cfg = CONFIGS["long4k_bf16"].with_(**shape)
     q, k, v, mask, _s = make_inputs(cfg, device="cpu")
     assert mab.selected_impl(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
