@@ -160,6 +160,41 @@ int ma_fwd(const ma_fwd_params* p, void* stream);
  *   - p->status may be NULL (device-side failures are then not reported). */
 int ma_fwd_noalloc(const ma_fwd_params* p, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Backward pass.  The reference trains through PyTorch autograd over
+ * monarch_attention_torch (ma/ma_torch.py:65-108; BART fine-tuning,
+ * bart/run_summarization.py); ma_bwd() computes the same gradients
+ * d<out, dout>/d(q, k, v) with CUDA kernels: the forward is recomputed with
+ * every step's intermediates kept (same rounding points as ma_fwd's generic
+ * kernels), then each phase is differentiated in reverse order.
+ *   - fwd: the forward call's parameters (q, k, v, mask, sizes, dtype f32 /
+ *     f16 / bf16; fwd.out, fwd.workspace and fwd.impl are not used).
+ *   - dout: the gradient of the (E, H, N, Dv) output, element strides.
+ *   - dq, dk, dv: receive the gradients in the input dtype, element strides.
+ *   - Nothing allocates; the workspace is ma_bwd_workspace_bytes() bytes.
+ * ------------------------------------------------------------------------ */
+typedef struct {
+  uint32_t struct_size; /* sizeof(ma_bwd_params)                          */
+  ma_fwd_params fwd;
+  const void* dout;
+  int64_t dout_stride[4];
+  void* dq;
+  void* dk;
+  void* dv;
+  int64_t dq_stride[4];
+  int64_t dk_stride[4];
+  int64_t dv_stride[4];
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t reserved[8];
+} ma_bwd_params;
+
+/* Bytes of workspace ma_bwd() needs (0 on bad params). */
+size_t ma_bwd_workspace_bytes(const ma_bwd_params* p);
+
+/* Enqueue the backward pass on `stream`; return codes as ma_fwd(). */
+int ma_bwd(const ma_bwd_params* p, void* stream);
+
 /* Which implementation ma_fwd() would run for these params
  * (MA_IMPL_GENERIC, MA_IMPL_TC or MA_IMPL_SMALL), or a negative error code. */
 int ma_select_impl(const ma_fwd_params* p);

@@ -38,6 +38,8 @@ EXPORTED = (
     "ma_read_status",
     "ma_last_launch_count",
     "ma_api_version",
+    "ma_bwd_workspace_bytes",
+    "ma_bwd",
 )
 
 _i64x4 = ctypes.c_int64 * 4
@@ -86,6 +88,31 @@ class MaFwdParams(ctypes.Structure):
         self.struct_size = ctypes.sizeof(MaFwdParams)
 
 
+class MaBwdParams(ctypes.Structure):
+    """Mirror of ``ma_bwd_params`` (include/ma_api.h)."""
+
+    _fields_ = [
+        ("struct_size", ctypes.c_uint32),
+        ("fwd", MaFwdParams),
+        ("dout", ctypes.c_void_p),
+        ("dout_stride", _i64x4),
+        ("dq", ctypes.c_void_p),
+        ("dk", ctypes.c_void_p),
+        ("dv", ctypes.c_void_p),
+        ("dq_stride", _i64x4),
+        ("dk_stride", _i64x4),
+        ("dv_stride", _i64x4),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+        ("reserved", ctypes.c_int32 * 8),
+    ]
+
+    def __init__(self, **kw):
+        super().__init__(**kw)
+        self.struct_size = ctypes.sizeof(MaBwdParams)
+        self.fwd.struct_size = ctypes.sizeof(MaFwdParams)
+
+
 _lib = None
 _lock = threading.Lock()
 
@@ -125,6 +152,11 @@ def load() -> ctypes.CDLL:
         lib.ma_last_launch_count.restype = ctypes.c_int
         lib.ma_api_version.argtypes = []
         lib.ma_api_version.restype = ctypes.c_int
+        PB = ctypes.POINTER(MaBwdParams)
+        lib.ma_bwd_workspace_bytes.argtypes = [PB]
+        lib.ma_bwd_workspace_bytes.restype = ctypes.c_size_t
+        lib.ma_bwd.argtypes = [PB, ctypes.c_void_p]
+        lib.ma_bwd.restype = ctypes.c_int
         _lib = lib
         return lib
 

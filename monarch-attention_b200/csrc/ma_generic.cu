@@ -362,6 +362,64 @@ static cudaError_t run_generic_t(GenParams gp, int T, cudaStream_t st, int* nlau
   return cudaSuccess;
 }
 
+// The forward's R and L phases with every step's intermediates kept (the
+// backward pass recomputes the forward this way): R-step t reads ar[t] /
+// cr[t] (t >= 1; step 0 reads q and cr = 1) and writes al[t] / cl[t] (and y
+// at t = T-1); L-step t writes ar[t+1] / cr[t+1].  No output phase.
+template <typename TI, typename TS>
+static cudaError_t run_generic_saved_t(GenParams gp, int T, char* const* al, float* const* cl,
+                                       char* const* ar, float* const* cr, cudaStream_t st,
+                                       int* nlaunch) {
+  cudaError_t err;
+  for (int t = 0; t < T; ++t) {
+    gp.first = (t == 0);
+    gp.al = al[t];
+    gp.cl = cl[t];
+    gp.ar = t > 0 ? ar[t] : ar[1 < T ? 1 : 0];  // unused at t = 0
+    gp.cr = t > 0 ? cr[t] : cr[1 < T ? 1 : 0];
+    if (t == T - 1) {
+      if ((err = launch_phase<PH_RF, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
+      *nlaunch += 1;
+      break;
+    }
+    if ((err = launch_phase<PH_R, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
+    gp.ar = ar[t + 1];
+    gp.cr = cr[t + 1];
+    if ((err = launch_phase<PH_LS, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
+    if ((err = launch_phase<PH_LA, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
+    *nlaunch += 3;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t run_generic_saved(const ma_fwd_params* p, const Shape& s, char* const* al,
+                              float* const* cl, char* const* ar, float* const* cr, char* y,
+                              float* lmax, float* lsum, cudaStream_t st, int* nlaunch) {
+  GenParams gp{};
+  gp.q = p->q; gp.k = p->k; gp.v = p->v; gp.out = nullptr;
+  for (int i = 0; i < 4; ++i) {
+    gp.qs[i] = p->q_stride[i]; gp.ks[i] = p->k_stride[i];
+    gp.vs[i] = p->v_stride[i]; gp.os[i] = 0;
+  }
+  gp.mask = p->mask_dtype == MA_MASK_NONE ? nullptr : p->mask;
+  gp.ms[0] = p->mask_stride[0]; gp.ms[1] = p->mask_stride[1];
+  gp.mask_dtype = p->mask_dtype;
+  gp.E = s.E; gp.H = s.H; gp.N = s.N; gp.D = s.D; gp.Dv = s.Dv; gp.b = s.b; gp.M = s.M;
+  gp.pad_off = s.pad_off; gp.sm_scale = s.sm_scale;
+  gp.y = y;
+  gp.lmax = lmax;
+  gp.lsum = lsum;
+  switch (p->dtype) {
+    case MA_DTYPE_F32: return run_generic_saved_t<float, float>(gp, s.T, al, cl, ar, cr, st, nlaunch);
+    case MA_DTYPE_F16:
+      return run_generic_saved_t<__half, __half>(gp, s.T, al, cl, ar, cr, st, nlaunch);
+    case MA_DTYPE_BF16:
+      return run_generic_saved_t<__nv_bfloat16, __nv_bfloat16>(gp, s.T, al, cl, ar, cr, st,
+                                                               nlaunch);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 // Limits of the generic path (checked by the C ABI before launching).
 bool generic_supports(const Shape& s) {
   if (s.D > 1024) return false;

@@ -20,8 +20,8 @@ dit/attention_processor.py:143); those calls work unchanged.  The work runs
 on the current CUDA stream through ``ma_fwd`` (include/ma_api.h).  Tensors on
 any other device raise: there is no CPU path.  With inputs that require
 gradients (training, e.g. the BART fine-tuning of the reference) the forward
-still runs on the kernels and the backward recomputes it with autograd
-(``training.py``), as the reference's own training path does.
+runs on the forward kernels and the backward on the backward kernels
+(``ma_bwd``, ``training.py``).
 """
 from __future__ import annotations
 
@@ -272,7 +272,7 @@ def monarch_attention(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None,
         if out is not None:
             raise ValueError("out= cannot be used when gradients are required")
         res = training.MonarchAttentionFunction.apply(q, k, v, attn_mask, T, B, pre_pad, impl,
-                                                      _kernel_forward)
+                                                      _kernel_forward, _kernel_backward)
     else:
         res = _kernel_forward(q, k, v, attn_mask, T, B, pre_pad, impl, scales, out)
     if check:
@@ -324,6 +324,35 @@ def _kernel_forward(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T
     _lib.check(rc)
     del keep
     return out
+
+
+def _kernel_backward(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int, B: int,
+                     pre_pad: bool, g: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """One ``ma_bwd`` call on the current stream: d<out, g>/d(q, k, v)."""
+    _check_previous(q.device)
+    lib = _lib.load()
+    g = g.to(v.dtype)
+    fp, keep = build_params(q, k, v, g, attn_mask, T, B, pre_pad)
+    bp = _lib.MaBwdParams()
+    bp.fwd = fp
+    bp.dout = g.data_ptr()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    for name, t in (("dout_stride", g), ("dq_stride", dq), ("dk_stride", dk), ("dv_stride", dv)):
+        arr = getattr(bp, name)
+        for i, st in enumerate(t.stride()):
+            arr[i] = st
+    bp.dq, bp.dk, bp.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    nbytes = lib.ma_bwd_workspace_bytes(ctypes.byref(bp))
+    if nbytes == 0:
+        _lib.check(lib.ma_bwd(ctypes.byref(bp), None))  # raises with the reason
+    with torch.cuda.device(q.device):
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        bp.workspace, bp.workspace_bytes = ws.data_ptr(), nbytes
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        rc = lib.ma_bwd(ctypes.byref(bp), ctypes.c_void_p(stream))
+    _lib.check(rc)
+    del keep
+    return dq, dk, dv
 
 
 def selected_impl(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: int, B: int,

@@ -1,7 +1,8 @@
-"""Backward pass: the torch restatement of the forward that the backward
-recomputes (monarch-attention_b200/training.py), pinned to the reference's
-own outputs and gradients (tests/golden, tests/golden/grad), and the CUDA
-forward + recomputed backward on the GPU."""
+"""Backward pass.  The gradient checker -- a torch restatement of the
+reference forward (oracle/ma_grad_oracle.py) -- is pinned to the reference's
+own outputs and gradients (tests/golden, tests/golden/grad); the CUDA
+backward (ma_bwd, through MonarchAttentionFunction) is compared with the
+reference fixtures and with autograd over the checker on the GPU."""
 import glob
 import os
 
@@ -13,7 +14,7 @@ from conftest import GOLDEN, golden_paths
 from gen_golden import load_case
 import monarch_attention_b200 as mab
 from monarch_attention_b200 import MonarchAttention, PadType, monarch_attention
-from monarch_attention_b200.training import torch_forward
+from oracle.ma_grad_oracle import torch_forward
 
 GRAD_DIR = os.path.join(GOLDEN, "grad")
 TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
@@ -145,3 +146,78 @@ def test_gradients_refuse_out_argument(cuda_device):
     q = torch.randn(1, 1, 16, 8, device=cuda_device, requires_grad=True)
     with pytest.raises(ValueError, match="out="):
         monarch_attention(q, q, q, None, 2, 4, False, out=torch.empty(1, 1, 16, 8, device=cuda_device))
+
+
+# The CUDA backward against autograd over the checker (same device, same
+# inputs): masks (bool, float), front and back padding, T = 1, 2, 3, Dv != D,
+# and the BART / RoBERTa / long shapes reduced to a few heads.
+BWD_CASES = [
+    ("t2_b16_f32", dict(E=2, H=2, N=256, D=64, Dv=64, B=16, T=2, pre=False, mask=None), "f32"),
+    ("t3_prepad_mask_f32", dict(E=2, H=1, N=197, D=64, Dv=64, B=14, T=3, pre=True,
+                                mask="bool"), "f32"),
+    ("t1_postpad_dv_f32", dict(E=1, H=2, N=100, D=32, Dv=48, B=16, T=1, pre=False, mask=None),
+     "f32"),
+    ("roberta_mask_f32", dict(E=2, H=2, N=512, D=64, Dv=64, B=32, T=2, pre=False,
+                              mask="float"), "f32"),
+    ("bart2k_mask_f32", dict(E=1, H=2, N=2048, D=64, Dv=64, B=32, T=2, pre=False,
+                             mask="float"), "f32"),
+    ("long4k_f32", dict(E=1, H=1, N=4096, D=128, Dv=128, B=64, T=2, pre=False, mask=None),
+     "f32"),
+    ("roberta_mask_bf16", dict(E=2, H=2, N=512, D=64, Dv=64, B=32, T=2, pre=False,
+                               mask="float"), "bf16"),
+    ("dit_f16", dict(E=1, H=2, N=1024, D=72, Dv=72, B=32, T=3, pre=False, mask=None), "f16"),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name,sh,dt", BWD_CASES, ids=[c[0] for c in BWD_CASES])
+def test_cuda_backward_matches_autograd_of_the_checker(name, sh, dt, cuda_device):
+    g = torch.Generator(device="cpu").manual_seed(31)
+    E, H, N, D, Dv = sh["E"], sh["H"], sh["N"], sh["D"], sh["Dv"]
+    s = 1.0 / np.sqrt(D)
+    q, k = (torch.randn(E, H, N, D, generator=g) * s for _ in range(2))
+    v = torch.randn(E, H, N, Dv, generator=g) * s
+    w = torch.randn(E, H, N, Dv, generator=g)
+    mask = None
+    if sh["mask"] is not None:
+        lens = torch.randint(N // 3, N, (E,), generator=g)
+        mask = torch.arange(N)[None, :] < lens[:, None]
+        if sh["mask"] == "float":
+            mask = mask.float()
+        mask = mask.to(cuda_device)
+    tdt = TORCH_DT[dt]
+    q, k, v, w = (t.to(cuda_device, tdt) for t in (q, k, v, w))
+    leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    out = monarch_attention(*leaves, mask, sh["T"], sh["B"], sh["pre"])
+    out.backward(w)
+    assert mab.read_status(cuda_device) == 0
+    ref_leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    ref_out = torch_forward(*ref_leaves, mask, sh["T"], sh["B"], sh["pre"])
+    ref = torch.autograd.grad(ref_out, ref_leaves, w)
+    for gname, got, r in zip(("dq", "dk", "dv"), leaves, ref):
+        r = r.float()
+        scale = float(r.abs().max())
+        tol = (1e-4 if dt == "f32" else 3e-2) * scale
+        err = float((got.grad.float() - r).abs().max())
+        assert torch.isfinite(got.grad).all()
+        assert err <= tol, f"{name} {gname}: max|err|={err:.3g} (max|ref|={scale:.3g})"
+
+
+def test_backward_abi_rejects_on_the_host():
+    """ma_bwd refuses bad parameters before any CUDA call (no GPU needed)."""
+    import ctypes
+    from monarch_attention_b200 import _lib
+    lib = mab.load_library()
+    bp = _lib.MaBwdParams()
+    assert lib.ma_bwd(ctypes.byref(bp), None) != 0  # forward block unset: invalid
+    f = bp.fwd
+    f.E, f.H, f.N, f.D, f.Dv = 1, 1, 64, 32, 32
+    f.block_size, f.num_steps = 8, 2
+    f.dtype = f.out_dtype = _lib.DTYPE_E4M3
+    f.out_dtype = _lib.DTYPE_BF16
+    assert lib.ma_bwd(ctypes.byref(bp), None) == 3  # e4m3: no gradients
+    f.dtype = f.out_dtype = _lib.DTYPE_BF16
+    assert lib.ma_bwd_workspace_bytes(ctypes.byref(bp)) > 0
+    assert lib.ma_bwd(ctypes.byref(bp), None) == 1  # NULL tensors
+    bp.struct_size = 4
+    assert lib.ma_bwd(ctypes.byref(bp), None) == 9
