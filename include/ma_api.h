@@ -63,8 +63,10 @@ typedef enum {
 typedef enum {
   MA_IMPL_AUTO = 0,
   MA_IMPL_GENERIC = 1, /* any shape/dtype: phase kernels, SIMT fp32 math   */
-  MA_IMPL_TC = 2,      /* tcgen05/TMEM kernels (b = M in {64, 128, 256})     */
-  MA_IMPL_SMALL = 3    /* fused per-head mma.sync kernel (b, M <= 32)       */
+  MA_IMPL_TC = 2,      /* tcgen05/TMEM kernels (b, M in {32, 64, 128}, D in
+                          {64, 128}; b = M = 256, D = 128)                 */
+  MA_IMPL_SMALL = 3    /* fused per-head kernels (b, M <= 32): mma.sync for
+                          16-bit, FFMA for fp32                            */
 } ma_impl_t;
 
 /* Return codes. */
@@ -109,7 +111,7 @@ typedef struct {
   int32_t num_steps;  /* T >= 1                                           */
   int32_t pre_pad;    /* 1: pad the front of the sequence                 */
   int32_t dtype;      /* ma_dtype_t of q, k, v                            */
-  int32_t out_dtype;  /* = dtype, or MA_DTYPE_BF16 when dtype is E4M3      */
+  int32_t out_dtype;  /* = dtype; MA_DTYPE_BF16 for E4M3; F32 with v_f32  */
   /* E4M3 only: per-(e,h) dequantisation scales, E*H floats each          */
   const float* q_scale;
   const float* k_scale;
@@ -119,7 +121,11 @@ typedef struct {
   size_t workspace_bytes;
   uint32_t* status; /* device word; bits MA_STATUS_* are OR-ed in          */
   int32_t impl;     /* ma_impl_t                                          */
-  int32_t reserved0;
+  /* 1: v and out are fp32 while q, k are fp16 / bf16 (the reference's
+   * get_matrix passes an fp32 identity as the values whatever the query
+   * dtype, ma/monarch_attention.py:60-70): y and the output step then run in
+   * fp32 (generic kernels).  0: v and out in the q / k dtype.              */
+  int32_t v_f32;
   /* optional (NULL = none): a word of page-locked host memory that the
    * device can write (cudaHostAlloc / cudaMallocHost, same address on host
    * and device).  A kernel that sets a status bit also stores that bit here

@@ -78,7 +78,7 @@ class MaFwdParams(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t),
         ("status", ctypes.c_void_p),
         ("impl", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("v_f32", ctypes.c_int32),
         ("status_host", ctypes.c_void_p),
         ("reserved", ctypes.c_int32 * 4),
     ]

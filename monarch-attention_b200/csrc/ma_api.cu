@@ -95,17 +95,20 @@ Shape make_shape(const ma_fwd_params* p) {
 // al / y / ar / cl / cr arrays, needs no lmax / lsum, and takes a token
 // validity bitmap of valid_bytes when masked; every other kernel keeps the
 // arrays of all E * H heads.
-WsLayout make_layout(const Shape& s, int dtype, bool conv, int impl, size_t valid_bytes) {
+WsLayout make_layout(const Shape& s, int dtype, bool conv, int impl, size_t valid_bytes,
+                     bool v_f32) {
   WsLayout w{};
-  // intermediates are kept in the input precision; e4m3 inputs use bf16
+  // intermediates are kept in the input precision; e4m3 inputs use bf16;
+  // y is kept in fp32 when the values are fp32 (v_f32)
   w.store_bytes = dtype == MA_DTYPE_F32 ? 4 : 2;
+  const int y_bytes = v_f32 ? 4 : w.store_bytes;
   const bool tc = impl == MA_IMPL_TC;
   const bool persistent = tc && s.b != 256;
   const size_t heads = persistent ? (size_t)tc_slots(s) : (size_t)s.E * s.H;
   const size_t bm = (size_t)s.b * s.M;
   size_t off = 0;
   w.al = off; off = align_up(off + heads * bm * s.D * w.store_bytes, 256);
-  w.y = off; off = align_up(off + heads * bm * s.Dv * w.store_bytes, 256);
+  w.y = off; off = align_up(off + heads * bm * s.Dv * y_bytes, 256);
   w.ar = off; off = align_up(off + heads * bm * s.D * w.store_bytes, 256);
   w.cl = off; off = align_up(off + heads * bm * 4, 256);
   w.cr = off; off = align_up(off + heads * bm * 4, 256);
@@ -171,7 +174,10 @@ int validate(const ma_fwd_params* p, bool need_buffers) {
   if (p->num_steps < 1)
     return fail(MA_ERR_BAD_SHAPE, "num_steps must be >= 1");
   if (elem_bytes(p->dtype) == 0) return fail(MA_ERR_BAD_DTYPE, "unknown q/k/v dtype");
-  const int want_out = p->dtype == MA_DTYPE_E4M3 ? MA_DTYPE_BF16 : p->dtype;
+  if (p->v_f32 && p->dtype != MA_DTYPE_F16 && p->dtype != MA_DTYPE_BF16)
+    return fail(MA_ERR_BAD_DTYPE, "v_f32 needs fp16 / bf16 q and k");
+  const int want_out = p->v_f32 ? MA_DTYPE_F32
+                                : (p->dtype == MA_DTYPE_E4M3 ? MA_DTYPE_BF16 : p->dtype);
   if (p->out_dtype != want_out)
     return fail(MA_ERR_BAD_DTYPE, "out_dtype must equal the value dtype (bf16 for e4m3)");
   if (p->mask_dtype < MA_MASK_NONE || p->mask_dtype > MA_MASK_BF16)
@@ -202,6 +208,14 @@ int validate(const ma_fwd_params* p, bool need_buffers) {
 // e4m3 problems are checked as their bf16 view (`view`): the tensor-core
 // kernels run them after a conversion launch, the generic kernels directly.
 int select_impl(const ma_fwd_params* p, const Shape& s, int* impl) {
+  if (p->v_f32) {  // fp32 values with 16-bit q / k: the generic kernels only
+    if (p->impl == MA_IMPL_TC || p->impl == MA_IMPL_SMALL)
+      return fail(MA_ERR_UNSUPPORTED, "fp32 values with 16-bit q / k run on the generic kernels");
+    if (!generic_supports(s))
+      return fail(MA_ERR_UNSUPPORTED, "shape exceeds the generic kernel's limits");
+    *impl = MA_IMPL_GENERIC;
+    return MA_OK;
+  }
   if (p->dtype == MA_DTYPE_E4M3 && p->impl != MA_IMPL_GENERIC) {
     const ma_fwd_params v = bf16_view(p, s, nullptr, WsLayout{});
     // the view has no buffers yet; the output pointer is the caller's
@@ -270,7 +284,7 @@ size_t ma_workspace_bytes(const ma_fwd_params* p) {
   g_detail = keep;
   if (rc != MA_OK) return 0;
   const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
-  return make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s)).total;
+  return make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s), p->v_f32 != 0).total;
 }
 
 int ma_select_impl(const ma_fwd_params* p) {
@@ -292,7 +306,7 @@ int ma_fwd(const ma_fwd_params* p, void* stream) {
   rc = select_impl(p, s, &impl);
   if (rc != MA_OK) return rc;
   const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
-  const WsLayout ws = make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s));
+  const WsLayout ws = make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s), p->v_f32 != 0);
   if (p->workspace == nullptr || p->workspace_bytes < ws.total)
     return fail(MA_ERR_WORKSPACE, "workspace needs " + std::to_string(ws.total) + " bytes, got " +
                                       std::to_string(p->workspace_bytes));

@@ -652,6 +652,10 @@ int bwd_check(const ma_bwd_params* p) {
     ma::set_error_detail("gradients through float8 e4m3 inputs are not supported");
     return MA_ERR_BAD_DTYPE;
   }
+  if (f->v_f32) {
+    ma::set_error_detail("gradients with fp32 values and 16-bit q / k are not supported");
+    return MA_ERR_UNSUPPORTED;
+  }
   const ma::Shape s = bwd_shape(f);
   if (s.D > ma::bwd::kMaxDim || s.Dv > ma::bwd::kMaxDim || s.b > ma::bwd::kMaxDim ||
       s.M > ma::bwd::kMaxDim || s.T > 64 || !ma::generic_supports(s)) {

@@ -90,7 +90,11 @@ __device__ __forceinline__ float load_tok(const void* base, const int64_t* st, c
   return x;
 }
 
-template <int PH, typename TI, typename TS, typename TO>
+// TI: q / k input type; TS: storage of al / ar and the rounding of the R / L
+// weights; TVI: v input type; TY: storage of y, the output type, and the
+// rounding of the y / output weights (the reference computes y = r.to(v.dtype)
+// @ v and z = l.to(y.dtype) @ y, ma_torch.py:51, 60).
+template <int PH, typename TI, typename TS, typename TVI, typename TY>
 __global__ void __launch_bounds__(GT) generic_phase_kernel(const GenParams p) {
   extern __shared__ float smem[];
   const int D = p.D;
@@ -111,7 +115,7 @@ __global__ void __launch_bounds__(GT) generic_phase_kernel(const GenParams p) {
   const int b = p.b, M = p.M;
 
   const TS* al_h = reinterpret_cast<const TS*>(p.al) + (size_t)eh * b * M * D;
-  const TS* y_h = reinterpret_cast<const TS*>(p.y) + (size_t)eh * b * M * p.Dv;
+  const TY* y_h = reinterpret_cast<const TY*>(p.y) + (size_t)eh * b * M * p.Dv;
   const TS* ar_h = reinterpret_cast<const TS*>(p.ar) + (size_t)eh * M * b * D;
   const float* cl_h = p.cl + (size_t)eh * b * M;
   const float* cr_h = p.cr + (size_t)eh * M * b;
@@ -243,13 +247,13 @@ __global__ void __launch_bounds__(GT) generic_phase_kernel(const GenParams p) {
         float w = srow[c] / den;
         w = fmaxf(w, kTiny);  // :18
         cl += w * logf(w);    // xlogy(r, r), :20
-        srow[c] = rnd<TS>(w);
+        srow[c] = w;          // rounded where it becomes a matmul operand
       }
 #pragma unroll
       for (int o = 16; o; o >>= 1) cl += __shfl_xor_sync(0xffffffffu, cl, o);
       if (lane == 0 && r < R) p.cl[(size_t)eh * b * M + (size_t)r * M + item] = cl;
-    } else {  // PH_O
-      for (int c = lane; c < C; c += 32) srow[c] = rnd<TS>(srow[c] / s);
+    } else {  // PH_O: l.to(y.dtype), :60
+      for (int c = lane; c < C; c += 32) srow[c] = rnd<TY>(srow[c] / s);
     }
   }
   if (PH == PH_LS) return;
@@ -272,11 +276,11 @@ __global__ void __launch_bounds__(GT) generic_phase_kernel(const GenParams p) {
           if (c < C && xd < X) {
             if (rphase) {
               x = seg == 0 ? load_tok<TI>(p.k, p.ks, p.ksc, p, e, h, item * b + c, xd)
-                           : load_tok<TI>(p.v, p.vs, p.vsc, p, e, h, item * b + c, xd);
+                           : load_tok<TVI>(p.v, p.vs, p.vsc, p, e, h, item * b + c, xd);
             } else if (PH == PH_LA) {
               x = load_tok<TI>(p.q, p.qs, p.qsc, p, e, h, c * b + item, xd);
             } else {
-              x = to_f<TS>(y_h[((size_t)item * M + c) * p.Dv + xd]);
+              x = to_f<TY>(y_h[((size_t)item * M + c) * p.Dv + xd]);
             }
           }
           Bs[cc * bstride + d] = x;
@@ -290,7 +294,9 @@ __global__ void __launch_bounds__(GT) generic_phase_kernel(const GenParams p) {
           for (int qd = 0; qd < 4; ++qd) xv[qd] = xrow[lane + 32 * qd];
 #pragma unroll
           for (int i = 0; i < RW; ++i) {
-            const float w = Sw[(warp * RW + i) * C + c0 + cc];
+            float w = Sw[(warp * RW + i) * C + c0 + cc];
+            // R-steps: r.to(k.dtype) for al, r.to(v.dtype) for y (:21, :51)
+            if (rphase) w = seg == 0 ? rnd<TS>(w) : rnd<TY>(w);
 #pragma unroll
             for (int qd = 0; qd < 4; ++qd) acc[i][qd] = fmaf(w, xv[qd], acc[i][qd]);
           }
@@ -309,17 +315,17 @@ __global__ void __launch_bounds__(GT) generic_phase_kernel(const GenParams p) {
             TS* al = reinterpret_cast<TS*>(p.al) + (size_t)eh * b * M * D;
             al[((size_t)r * M + item) * D + xd] = from_f<TS>(p.sm_scale * rnd<TS>(a));
           } else if (rphase) {  // y = r @ v, :51
-            TS* y = reinterpret_cast<TS*>(p.y) + (size_t)eh * b * M * p.Dv;
-            y[((size_t)r * M + item) * p.Dv + xd] = from_f<TS>(a);
+            TY* y = reinterpret_cast<TY*>(p.y) + (size_t)eh * b * M * p.Dv;
+            y[((size_t)r * M + item) * p.Dv + xd] = from_f<TY>(a);
           } else if (PH == PH_LA) {  // ar = l @ q, :34
             TS* ar = reinterpret_cast<TS*>(p.ar) + (size_t)eh * M * b * D;
             ar[((size_t)r * b + item) * D + xd] = from_f<TS>(a);
           } else {  // z = l @ y, written at token l*b + j (unpadded), :60-62, :106-108
             const int n = r * b + item - p.pad_off;
             if (n >= 0 && n < p.N) {
-              TO* o = reinterpret_cast<TO*>(p.out);
+              TY* o = reinterpret_cast<TY*>(p.out);
               o[(int64_t)e * p.os[0] + (int64_t)h * p.os[1] + (int64_t)n * p.os[2] +
-                (int64_t)xd * p.os[3]] = from_f<TO>(a);
+                (int64_t)xd * p.os[3]] = from_f<TY>(a);
             }
           }
         }
@@ -331,12 +337,12 @@ __global__ void __launch_bounds__(GT) generic_phase_kernel(const GenParams p) {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-template <int PH, typename TI, typename TS, typename TO>
+template <int PH, typename TI, typename TS, typename TVI, typename TY>
 static cudaError_t launch_phase(const GenParams& gp, cudaStream_t st) {
   const int R = (PH == PH_R || PH == PH_RF) ? gp.b : gp.M;
   const int items = (PH == PH_R || PH == PH_RF) ? gp.M : gp.b;
   const size_t smem = generic_smem_bytes(gp.D, R);
-  auto kfn = generic_phase_kernel<PH, TI, TS, TO>;
+  auto kfn = generic_phase_kernel<PH, TI, TS, TVI, TY>;
   cudaError_t err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
   if (err != cudaSuccess) return err;
@@ -345,19 +351,19 @@ static cudaError_t launch_phase(const GenParams& gp, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-template <typename TI, typename TS, typename TO>
+template <typename TI, typename TS, typename TVI, typename TY>
 static cudaError_t run_generic_t(GenParams gp, int T, cudaStream_t st, int* nlaunch) {
   cudaError_t err;
   for (int t = 0; t < T - 1; ++t) {
     gp.first = (t == 0);
-    if ((err = launch_phase<PH_R, TI, TS, TO>(gp, st)) != cudaSuccess) return err;
-    if ((err = launch_phase<PH_LS, TI, TS, TO>(gp, st)) != cudaSuccess) return err;
-    if ((err = launch_phase<PH_LA, TI, TS, TO>(gp, st)) != cudaSuccess) return err;
+    if ((err = launch_phase<PH_R, TI, TS, TVI, TY>(gp, st)) != cudaSuccess) return err;
+    if ((err = launch_phase<PH_LS, TI, TS, TVI, TY>(gp, st)) != cudaSuccess) return err;
+    if ((err = launch_phase<PH_LA, TI, TS, TVI, TY>(gp, st)) != cudaSuccess) return err;
     *nlaunch += 3;
   }
   gp.first = (T == 1);
-  if ((err = launch_phase<PH_RF, TI, TS, TO>(gp, st)) != cudaSuccess) return err;
-  if ((err = launch_phase<PH_O, TI, TS, TO>(gp, st)) != cudaSuccess) return err;
+  if ((err = launch_phase<PH_RF, TI, TS, TVI, TY>(gp, st)) != cudaSuccess) return err;
+  if ((err = launch_phase<PH_O, TI, TS, TVI, TY>(gp, st)) != cudaSuccess) return err;
   *nlaunch += 2;
   return cudaSuccess;
 }
@@ -378,15 +384,15 @@ static cudaError_t run_generic_saved_t(GenParams gp, int T, char* const* al, flo
     gp.ar = t > 0 ? ar[t] : ar[1 < T ? 1 : 0];  // unused at t = 0
     gp.cr = t > 0 ? cr[t] : cr[1 < T ? 1 : 0];
     if (t == T - 1) {
-      if ((err = launch_phase<PH_RF, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
+      if ((err = launch_phase<PH_RF, TI, TS, TS, TS>(gp, st)) != cudaSuccess) return err;
       *nlaunch += 1;
       break;
     }
-    if ((err = launch_phase<PH_R, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
+    if ((err = launch_phase<PH_R, TI, TS, TS, TS>(gp, st)) != cudaSuccess) return err;
     gp.ar = ar[t + 1];
     gp.cr = cr[t + 1];
-    if ((err = launch_phase<PH_LS, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
-    if ((err = launch_phase<PH_LA, TI, TS, TS>(gp, st)) != cudaSuccess) return err;
+    if ((err = launch_phase<PH_LS, TI, TS, TS, TS>(gp, st)) != cudaSuccess) return err;
+    if ((err = launch_phase<PH_LA, TI, TS, TS, TS>(gp, st)) != cudaSuccess) return err;
     *nlaunch += 3;
   }
   return cudaSuccess;
@@ -452,13 +458,22 @@ cudaError_t run_generic(const ma_fwd_params* p, const Shape& s, const WsLayout& 
   gp.cr = reinterpret_cast<float*>(w + ws.cr);
   gp.lmax = reinterpret_cast<float*>(w + ws.lmax);
   gp.lsum = reinterpret_cast<float*>(w + ws.lsum);
+  if (p->v_f32) {  // fp32 values with 16-bit q / k (get_matrix)
+    if (p->dtype == MA_DTYPE_F16)
+      return run_generic_t<__half, __half, float, float>(gp, s.T, st, nlaunch);
+    if (p->dtype == MA_DTYPE_BF16)
+      return run_generic_t<__nv_bfloat16, __nv_bfloat16, float, float>(gp, s.T, st, nlaunch);
+    return cudaErrorInvalidValue;
+  }
   switch (p->dtype) {
-    case MA_DTYPE_F32: return run_generic_t<float, float, float>(gp, s.T, st, nlaunch);
-    case MA_DTYPE_F16: return run_generic_t<__half, __half, __half>(gp, s.T, st, nlaunch);
+    case MA_DTYPE_F32: return run_generic_t<float, float, float, float>(gp, s.T, st, nlaunch);
+    case MA_DTYPE_F16: return run_generic_t<__half, __half, __half, __half>(gp, s.T, st, nlaunch);
     case MA_DTYPE_BF16:
-      return run_generic_t<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(gp, s.T, st, nlaunch);
+      return run_generic_t<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(
+          gp, s.T, st, nlaunch);
     case MA_DTYPE_E4M3:
-      return run_generic_t<__nv_fp8_e4m3, __nv_bfloat16, __nv_bfloat16>(gp, s.T, st, nlaunch);
+      return run_generic_t<__nv_fp8_e4m3, __nv_bfloat16, __nv_fp8_e4m3, __nv_bfloat16>(
+          gp, s.T, st, nlaunch);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -209,6 +209,8 @@ def build_params(q: Tensor, k: Tensor, v: Tensor, out: Tensor, attn_mask: Tensor
     p.block_size, p.num_steps, p.pre_pad = int(B), int(T), int(bool(pre_pad))
     p.dtype = _TORCH_TO_MA[q.dtype]
     p.out_dtype = _TORCH_TO_MA[out.dtype]
+    # fp32 values with 16-bit q / k (the reference's get_matrix)
+    p.v_f32 = int(v.dtype == torch.float32 and q.dtype in (torch.float16, torch.bfloat16))
     keep = [q, k, v, out, mkeep]
     if scales is not None:
         qs, ks, vs = (s.to(device=q.device, dtype=torch.float32).contiguous() for s in scales)
@@ -225,8 +227,10 @@ def _check_inputs(q: Tensor, k: Tensor, v: Tensor) -> None:
         raise ValueError(f"key shape {tuple(k.shape)} != query shape {tuple(q.shape)}")
     if v.shape[:3] != q.shape[:3]:
         raise ValueError(f"value shape {tuple(v.shape)} does not match query {tuple(q.shape)}")
-    if not (q.dtype == k.dtype == v.dtype):
-        raise TypeError(f"query/key/value dtypes differ: {q.dtype}, {k.dtype}, {v.dtype}")
+    mixed = v.dtype == torch.float32 and q.dtype in (torch.float16, torch.bfloat16)
+    if not (q.dtype == k.dtype and (v.dtype == q.dtype or mixed)):
+        raise TypeError(f"query/key/value dtypes differ: {q.dtype}, {k.dtype}, {v.dtype} "
+                        "(fp32 values with fp16 / bf16 queries and keys are accepted)")
     if q.dtype not in _TORCH_TO_MA:
         raise TypeError(f"unsupported dtype {q.dtype}")
     for t in (q, k, v):
@@ -362,7 +366,8 @@ def selected_impl(q: Tensor, k: Tensor, v: Tensor, attn_mask: Tensor | None, T: 
     lib = _lib.load()
     out = torch.empty((1,), device=q.device)
     p, _keep = build_params(q, k, v, out, attn_mask, T, B, pre_pad, _impl_code(impl))
-    p.out_dtype = p.dtype if p.dtype != _lib.DTYPE_E4M3 else _lib.DTYPE_BF16
+    p.out_dtype = (_lib.DTYPE_F32 if p.v_f32 else
+                   p.dtype if p.dtype != _lib.DTYPE_E4M3 else _lib.DTYPE_BF16)
     for i, s in enumerate((q.shape[1] * q.shape[2] * v.shape[-1], q.shape[2] * v.shape[-1],
                            v.shape[-1], 1)):
         p.o_stride[i] = s
@@ -397,17 +402,17 @@ class MonarchAttention(nn.Module):
 
     def get_matrix(self, query: Tensor, key: Tensor,
                    attention_mask: Tensor | None = None) -> Tensor:
-        """Dense (E, H, N, N) attention matrix: the forward with V = I (fp32 result).
+        """Dense (E, H, N, N) attention matrix: the forward with V = I.
 
-        The reference passes a float32 identity whatever the query dtype
-        (ma/monarch_attention.py:67-69).  Here the identity is built in the
-        query dtype (0 and 1 are exact in every dtype), so the y / z products
-        are rounded to the query dtype, and the result is returned as fp32.
+        As in the reference (ma/monarch_attention.py:60-70) the identity is
+        fp32 whatever the query dtype, so with 16-bit queries the R / L steps
+        run in the query dtype and y and the output step in fp32; the result
+        is fp32.
         """
         batch_size, num_heads, seq_len, _ = query.shape
-        value = torch.eye(seq_len, device=query.device, dtype=query.dtype).expand(
+        value = torch.eye(seq_len, device=query.device, dtype=torch.float32).expand(
             batch_size, num_heads, seq_len, seq_len)
-        return self.forward(query, key, value, attention_mask).float()
+        return self.forward(query, key, value, attention_mask)
 
     def extra_repr(self) -> str:
         return (f"block_size={self.block_size}, num_steps={self.num_steps}, "

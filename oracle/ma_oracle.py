@@ -71,12 +71,14 @@ def _softmax(x: np.ndarray, axis: int) -> np.ndarray:
     return e / np.sum(e, axis=axis, keepdims=True)
 
 
-def _r_step(ar, k, v, cr, sm_scale, mask, dtype, want_y):
+def _r_step(ar, k, v, cr, sm_scale, mask, dtype, want_y, v_dtype=None):
     """R-step for every key block (ma/ma_torch.py:10-23, 38-52).
 
     ar, k: (..., M, B, D); v: (..., M, B, Dv) or None; cr: (..., M, B) fp32;
     mask: broadcastable to (..., M, B) bool (key validity).
     Returns al (..., B, M, D), cl (..., B, M), y (..., B, M, Dv) or None.
+    ``v_dtype`` (default ``dtype``): the value dtype, in which y = r.to(v.dtype)
+    @ v is computed (:51).
     """
     r_hat = np.float32(sm_scale) * _mm(ar, np.swapaxes(k, -1, -2), dtype)
     r_hat = r_hat / (cr[..., :, None] + np.float32(EPS))
@@ -92,7 +94,8 @@ def _r_step(ar, k, v, cr, sm_scale, mask, dtype, want_y):
     al = np.swapaxes(al, -2, -3)
     y = None
     if want_y:
-        y = np.swapaxes(_mm(r_op, v, dtype), -2, -3)
+        vd = v_dtype or dtype
+        y = np.swapaxes(_mm(round_to(r, vd), v, vd), -2, -3)
     return al, cl.astype(np.float32), y
 
 
@@ -112,12 +115,14 @@ def _l_step(al, q_t, cl, mask_t, dtype):
     return ar, cr.astype(np.float32)
 
 
-def _z_step(al, q_t, cl, y, dtype):
-    """Output step (ma/ma_torch.py:55-62): softmax over key blocks, times y."""
+def _z_step(al, q_t, cl, y, dtype, v_dtype=None):
+    """Output step (ma/ma_torch.py:55-62): softmax over key blocks, times y
+    (in the value dtype ``v_dtype``, default ``dtype``: l.to(y.dtype) @ y)."""
     l_hat = _mm(q_t, np.swapaxes(al, -1, -2), dtype)
     l_hat = l_hat - cl[..., None, :]
     l = _softmax(l_hat, axis=-1)
-    z = _mm(round_to(l, dtype), y, dtype)
+    vd = v_dtype or dtype
+    z = _mm(round_to(l, vd), y, vd)
     return np.swapaxes(z, -2, -3)
 
 
@@ -142,14 +147,17 @@ def validity_mask(E: int, N: int, B: int, pre_pad: bool, attn_mask=None) -> np.n
 
 
 def monarch_attention_oracle(q, k, v, attn_mask, T: int, B: int, pre_pad: bool,
-                             dtype: str = "f32") -> np.ndarray:
+                             dtype: str = "f32", v_dtype: str | None = None) -> np.ndarray:
     """MonarchAttention forward (ma/ma_torch.py:65-108) on CPU.
 
     q, k: (E, H, N, D); v: (E, H, N, Dv) float arrays whose values are already
     representable in ``dtype``.  attn_mask: None or (E, N), nonzero = valid.
-    Returns (E, H, N, Dv) float32 (values rounded to ``dtype``).
+    ``v_dtype`` (default ``dtype``): a different value dtype, as in the
+    reference's ``get_matrix`` (fp32 identity values with 16-bit queries,
+    ma/monarch_attention.py:60-70): y and z are then computed in it.
+    Returns (E, H, N, Dv) float32 (values rounded to the value dtype).
     """
-    if dtype not in DTYPES:
+    if dtype not in DTYPES or (v_dtype is not None and v_dtype not in DTYPES):
         raise ValueError(f"dtype must be one of {DTYPES}")
     q = np.asarray(q, dtype=np.float32)
     k = np.asarray(k, dtype=np.float32)
@@ -175,12 +183,13 @@ def monarch_attention_oracle(q, k, v, attn_mask, T: int, B: int, pre_pad: bool,
     for _ in range(T - 1):
         al, cl, _ = _r_step(ar, kb, None, cr, sm_scale, mask, dtype, False)
         ar, cr = _l_step(al, q_t, cl, mask_t, dtype)
-    al, cl, y = _r_step(ar, kb, vb, cr, sm_scale, mask, dtype, True)
-    z = _z_step(al, q_t, cl, y, dtype).reshape(E, H, Np, Dv)
+    al, cl, y = _r_step(ar, kb, vb, cr, sm_scale, mask, dtype, True, v_dtype)
+    z = _z_step(al, q_t, cl, y, dtype, v_dtype).reshape(E, H, Np, Dv)
     return z[:, :, Np - N:, :] if pre_pad else z[:, :, :N, :]
 
 
-def monarch_attention_oracle_heads(q, k, v, attn_mask, T, B, pre_pad, dtype="f32"):
+def monarch_attention_oracle_heads(q, k, v, attn_mask, T, B, pre_pad, dtype="f32",
+                                   v_dtype=None):
     """Same as :func:`monarch_attention_oracle`, one (e, h) at a time.
 
     Heads and batch rows never interact (ma/ma_torch.py mixes neither), so
@@ -194,7 +203,7 @@ def monarch_attention_oracle_heads(q, k, v, attn_mask, T, B, pre_pad, dtype="f32
         for h in range(H):
             out[e, h] = monarch_attention_oracle(
                 q[e:e + 1, h:h + 1], k[e:e + 1, h:h + 1], v[e:e + 1, h:h + 1],
-                am, T, B, pre_pad, dtype)[0, 0]
+                am, T, B, pre_pad, dtype, v_dtype)[0, 0]
     return out
 
 

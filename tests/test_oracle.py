@@ -1,5 +1,6 @@
 """The CPU oracle against the reference's own outputs (golden fixtures made by
 tests/golden/gen_golden.py running ma/ma_torch.py), plus structural checks."""
+import glob
 import os
 
 import numpy as np
@@ -130,3 +131,28 @@ def test_flop_count_matches_reference_figures(N, B, T, ref):
     3x the algorithmic count."""
     f = flops(1, 12, N, 64, 64, B, T) * 3
     assert abs(f - ref) / ref < 0.01
+
+
+MATRIX_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "matrix")
+
+
+def matrix_paths():
+    return sorted(glob.glob(os.path.join(MATRIX_DIR, "*.npz")))
+
+
+@pytest.mark.parametrize("path", matrix_paths(), ids=lambda p: os.path.basename(p)[:-4])
+def test_oracle_get_matrix_matches_reference(path):
+    """The reference's get_matrix (ma/monarch_attention.py:60-70) runs 16-bit
+    queries with fp32 identity values: y and z in fp32, the R / L steps in the
+    query dtype.  The oracle's value-dtype mode reproduces it (fixtures from
+    the reference itself, tests/golden/matrix/gen_matrix_golden.py)."""
+    import json
+    c = np.load(path)
+    m = json.loads(str(c["meta"]))
+    E, H, N = m["E"], m["H"], m["N"]
+    v = np.broadcast_to(np.eye(N, dtype=np.float32), (E, H, N, N))
+    mask = c["mask"] if "mask" in c else None
+    got = monarch_attention_oracle(c["q"], c["k"], v, mask, m["T"], m["B"], m["pre_pad"],
+                                   m["dtype"], "f32")
+    ref = c["matrix"]
+    assert np.abs(got - ref).max() <= 1e-6 * np.abs(ref).max()

@@ -6,6 +6,7 @@ fp32 reference; bf16 / fp16 within 2e-2 * max|ref| of the fp32 reference run
 on the same (rounded) inputs; e4m3 against the fp32 oracle on the
 dequantised inputs within E4M3_TOL * max|ref| (stated bound).
 """
+import glob
 import os
 
 import numpy as np
@@ -478,3 +479,29 @@ def test_e4m3_full_size_tc(cuda_device):
         got = out[sl].float().cpu().numpy()
         err = np.abs(got - ref).max()
         assert err <= E4M3_TOL * float(np.abs(ref).max()), f"head ({e},{h}): max|err|={err:.3g}"
+
+
+MATRIX_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "matrix")
+
+
+@pytest.mark.parametrize("path", sorted(glob.glob(os.path.join(MATRIX_DIR, "*.npz"))),
+                         ids=lambda p: os.path.basename(p)[:-4])
+def test_get_matrix_16bit_queries_match_reference(path, cuda_device):
+    """get_matrix with fp16 / bf16 queries: fp32 identity values, so y and
+    the output step run in fp32 like the reference's (fixtures of the
+    reference's own get_matrix, tests/golden/matrix)."""
+    import json
+    c = np.load(path)
+    m = json.loads(str(c["meta"]))
+    dt = TORCH_DT[m["dtype"]]
+    q, k = (torch.from_numpy(c[n]).to(cuda_device, dt) for n in ("q", "k"))
+    mask = None if "mask" not in c else torch.from_numpy(c["mask"]).to(cuda_device)
+    attn = MonarchAttention(m["B"], m["T"], PadType.pre if m["pre_pad"] else PadType.post)
+    A = attn.get_matrix(q, k, mask)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert A.dtype == torch.float32
+    ref = c["matrix"]
+    err = np.abs(A.cpu().numpy() - ref).max()
+    # the same rounding points; only fp32 summation order differs
+    assert err <= 1e-3 * np.abs(ref).max(), f"max|err|={err:.3g}"

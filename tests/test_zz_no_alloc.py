@@ -5,8 +5,9 @@ path that runs the attention (a runtime that owns the memory pool, a serving
 loop with a fixed device-memory budget): it takes only q / k / v / out and runs
 the tcgen05 kernel on a scratch array compiled into the library.  This file
 calls it through the C ABI, twice in a row on different inputs, and checks
-each result against the regular entry point on the same inputs, within the
-bf16 tolerance the other parity tests use (2e-2 * max|ref|).
+each result against the regular entry point on the same inputs, and one head
+of the second call against the CPU oracle, within the bf16 tolerance the
+other parity tests use (2e-2 * max|ref|).
 
 It is collected last (file name) so that a run stopping at the first failure
 has run every other test before it; it passes alone in a fresh process too.
@@ -55,6 +56,16 @@ def test_noalloc_matches_ma_fwd_twice(H, cuda_device):
         scale = ref.float().abs().max().item()
         err = (out.float() - ref.float()).abs().max().item()
         assert err <= LP_TOL * scale, f"call {call}: max|err|={err:.3g}"
+        if call == 1:
+            # and one head directly against the CPU oracle (fp32 reference)
+            from oracle.ma_oracle import monarch_attention_oracle_heads
+            h = H - 1
+            o = monarch_attention_oracle_heads(
+                *(t[:, h:h + 1].float().cpu().numpy() for t in (q, k, v)), None, cfg.T, cfg.B,
+                cfg.pre_pad, "f32")
+            got = out[:, h:h + 1].float().cpu().numpy()
+            oerr = float(abs(got - o).max())
+            assert oerr <= LP_TOL * float(abs(o).max()), f"oracle: max|err|={oerr:.3g}"
 
 
 @pytest.mark.gpu
