@@ -32,6 +32,7 @@ cudaError_t run_tc256(const ma_fwd_params* p, const Shape& s, const WsLayout& ws
 // ma_tc.cu
 bool tc_supports(const ma_fwd_params* p, const Shape& s);
 int tc_slots(const Shape& s);
+bool tc_fp8_direct(const ma_fwd_params* p, const Shape& s);
 size_t tc_ctrl_bytes(const Shape& s);
 size_t tc_valid_bytes(const ma_fwd_params* p, const Shape& s);
 cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, cudaStream_t st,
@@ -283,7 +284,7 @@ size_t ma_workspace_bytes(const ma_fwd_params* p) {
   const int rc = select_impl(p, s, &impl);
   g_detail = keep;
   if (rc != MA_OK) return 0;
-  const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
+  const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC && !tc_fp8_direct(p, s);
   return make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s), p->v_f32 != 0).total;
 }
 
@@ -305,7 +306,10 @@ int ma_fwd(const ma_fwd_params* p, void* stream) {
   int impl = 0;
   rc = select_impl(p, s, &impl);
   if (rc != MA_OK) return rc;
-  const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC;
+  // e4m3: the persistent tcgen05 kernel reads the e4m3 tiles itself where it
+  // can; otherwise a conversion launch writes bf16 copies first
+  const bool direct = p->dtype == MA_DTYPE_E4M3 && impl == MA_IMPL_TC && tc_fp8_direct(p, s);
+  const bool conv = p->dtype == MA_DTYPE_E4M3 && impl != MA_IMPL_GENERIC && !direct;
   const WsLayout ws = make_layout(s, p->dtype, conv, impl, tc_valid_bytes(p, s), p->v_f32 != 0);
   if (p->workspace == nullptr || p->workspace_bytes < ws.total)
     return fail(MA_ERR_WORKSPACE, "workspace needs " + std::to_string(ws.total) + " bytes, got " +

@@ -16,16 +16,28 @@ namespace ma {
 namespace tc {
 
 // explicit instantiations live in ma_tc_inst_*.cu
-#define MA_TC_DECLARE(BB, MM, DD)                                                              \
-  extern template cudaError_t launch_tc<true, BB, MM, DD, false>(const TcParams&, int,          \
-                                                                 cudaStream_t);                 \
-  extern template cudaError_t launch_tc<false, BB, MM, DD, false>(const TcParams&, int,         \
-                                                                  cudaStream_t);                \
-  extern template cudaError_t launch_tc<true, BB, MM, DD, true>(const TcParams&, int,           \
-                                                                cudaStream_t);                  \
-  extern template cudaError_t launch_tc<false, BB, MM, DD, true>(const TcParams&, int, cudaStream_t);
+#define MA_TC_DECLARE(BB, MM, DD)                                                          \
+  extern template cudaError_t launch_tc<true, BB, MM, DD, false, false>(const TcParams&,    \
+                                                                        int, cudaStream_t); \
+  extern template cudaError_t launch_tc<false, BB, MM, DD, false, false>(const TcParams&,   \
+                                                                         int, cudaStream_t);\
+  extern template cudaError_t launch_tc<true, BB, MM, DD, true, false>(const TcParams&, int, \
+                                                                       cudaStream_t);       \
+  extern template cudaError_t launch_tc<false, BB, MM, DD, true, false>(const TcParams&, int,\
+                                                                        cudaStream_t);
 MA_TC_SHAPES(MA_TC_DECLARE)
 #undef MA_TC_DECLARE
+// e4m3 inputs read directly (f16 arithmetic): head dim 128, b = M = 64 or 128
+#define MA_TC_FP8_SHAPES(X) \
+  X(128, 128, 128)          \
+  X(64, 64, 128)
+#define MA_TC_DECLARE8(BB, MM, DD)                                                          \
+  extern template cudaError_t launch_tc<false, BB, MM, DD, false, true>(const TcParams&,    \
+                                                                        int, cudaStream_t); \
+  extern template cudaError_t launch_tc<false, BB, MM, DD, true, true>(const TcParams&, int, \
+                                                                       cudaStream_t);
+MA_TC_FP8_SHAPES(MA_TC_DECLARE8)
+#undef MA_TC_DECLARE8
 
 static bool shape_compiled(int b, int M, int D) {
 #define MA_TC_MATCH(BB, MM, DD) \
@@ -35,15 +47,25 @@ static bool shape_compiled(int b, int M, int D) {
   return false;
 }
 
-static cudaError_t dispatch(bool bf16, int b, int M, int D, const TcParams& tp, int grid,
-                            cudaStream_t st) {
+static cudaError_t dispatch(bool bf16, bool fp8, int b, int M, int D, const TcParams& tp,
+                            int grid, cudaStream_t st) {
+  const bool masked = tp.valid != nullptr;
+  if (fp8) {
+#define MA_TC_CALL8(BB, MM, DD)                                                  \
+  if (b == BB && M == MM && D == DD)                                             \
+    return masked ? launch_tc<false, BB, MM, DD, true, true>(tp, grid, st)       \
+                  : launch_tc<false, BB, MM, DD, false, true>(tp, grid, st);
+    MA_TC_FP8_SHAPES(MA_TC_CALL8)
+#undef MA_TC_CALL8
+    return cudaErrorInvalidValue;
+  }
 #define MA_TC_CALL(BB, MM, DD)                                                              \
   if (b == BB && M == MM && D == DD) {                                                      \
-    if (tp.valid != nullptr)                                                                \
-      return bf16 ? launch_tc<true, BB, MM, DD, true>(tp, grid, st)                         \
-                  : launch_tc<false, BB, MM, DD, true>(tp, grid, st);                       \
-    return bf16 ? launch_tc<true, BB, MM, DD, false>(tp, grid, st)                          \
-                : launch_tc<false, BB, MM, DD, false>(tp, grid, st);                        \
+    if (masked)                                                                             \
+      return bf16 ? launch_tc<true, BB, MM, DD, true, false>(tp, grid, st)                  \
+                  : launch_tc<false, BB, MM, DD, true, false>(tp, grid, st);                \
+    return bf16 ? launch_tc<true, BB, MM, DD, false, false>(tp, grid, st)                   \
+                : launch_tc<false, BB, MM, DD, false, false>(tp, grid, st);                 \
   }
   MA_TC_SHAPES(MA_TC_CALL)
 #undef MA_TC_CALL
@@ -116,6 +138,32 @@ bool tc_supports(const ma_fwd_params* p, const Shape& s) {
   return true;
 }
 
+// e4m3 calls the persistent kernel reads directly (no bf16 copies): head dim
+// 128, b = M = 64 or 128, q / k / v rows of 128 bytes at 16-byte aligned
+// addresses.  MA_FP8_CONVERT=1 forces the conversion path instead.
+bool tc_fp8_direct(const ma_fwd_params* p, const Shape& s) {
+  if (p->dtype != MA_DTYPE_E4M3) return false;
+  const char* conv = getenv("MA_FP8_CONVERT");
+  if (conv && conv[0] == '1') return false;
+  const char* off = getenv("MA_DISABLE_TC");
+  if (off && off[0] == '1') return false;
+  if (s.D != 128 || s.Dv != 128 || s.N != s.Np || s.b != s.M || (s.b != 64 && s.b != 128))
+    return false;
+  const int64_t* st[3] = {p->q_stride, p->k_stride, p->v_stride};
+  for (int t = 0; t < 3; ++t) {
+    if (st[t][3] != 1) return false;
+    for (int i = 0; i < 3; ++i)
+      if (st[t][i] % 16 != 0 || st[t][i] <= 0) return false;
+  }
+  const int64_t* os = p->o_stride;  // bf16 output
+  if (os[3] != 1) return false;
+  for (int i = 0; i < 3; ++i)
+    if ((os[i] * 2) % 16 != 0 || os[i] <= 0) return false;
+  if (p->q && !(aligned16(p->q) && aligned16(p->k) && aligned16(p->v) && aligned16(p->out)))
+    return false;
+  return true;
+}
+
 // Heads per wavefront phase slot of the persistent kernel: more heads in
 // flight give a longer distance between dependent tiles (a round is
 // 2T * hgroup * tiles tiles).  Measured best on B200 for b = M = 128
@@ -158,8 +206,15 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   using namespace tc;
   TcParams tp;
   memset(&tp, 0, sizeof(tp));
+  // e4m3 inputs (read directly): byte tiles of q / k / v, f16 intermediates,
+  // bf16 output
+  const bool fp8 = p->dtype == MA_DTYPE_E4M3;
   const CUtensorMapDataType dt =
       p->dtype == MA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType dt_in = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : dt;
+  const CUtensorMapDataType dt_out = fp8 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : dt;
+  const uint64_t esz = fp8 ? 1 : 2;          // bytes per q / k / v element
+  const uint32_t in_box = fp8 ? 128u : 64u;  // elements per 128-byte row of a tile
   const int nheads = s.E * s.H;
   const int P = 2 * s.T;
   const int tiles = s.b * s.M / kT;  // tiles per (head, phase)
@@ -171,14 +226,15 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
     hgroup = max_slots / (2 * s.T + 1) > 1 ? max_slots / (2 * s.T + 1) : 1;
   int slots = hgroup * (2 * s.T + 1);
   if (slots > max_slots) slots = max_slots;
-  const uint32_t box_blk[4] = {64, kT, 1, 1};
-  const uint32_t box_str[5] = {64, 1, (uint32_t)s.M, 1, 1};
+  const uint32_t box_blk[4] = {in_box, kT, 1, 1};
+  const uint32_t box_str[5] = {in_box, 1, (uint32_t)s.M, 1, 1};
   const uint32_t box_ws[2] = {64, kT};
   bool ok = true;
   auto tok_map = [&](CUtensorMap* tm, const void* base, const int64_t* es) {
     const uint64_t dims[4] = {(uint64_t)s.D, (uint64_t)s.N, (uint64_t)s.H, (uint64_t)s.E};
-    const uint64_t str[3] = {(uint64_t)es[2] * 2, (uint64_t)es[1] * 2, (uint64_t)es[0] * 2};
-    ok = ok && encode(tm, dt, 4, base, dims, str, box_blk);
+    const uint64_t str[3] = {(uint64_t)es[2] * esz, (uint64_t)es[1] * esz,
+                             (uint64_t)es[0] * esz};
+    ok = ok && encode(tm, dt_in, 4, base, dims, str, box_blk);
   };
   tok_map(&tp.tm_qblk, p->q, p->q_stride);
   tok_map(&tp.tm_kblk, p->k, p->k_stride);
@@ -187,9 +243,9 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
     const int64_t* es = p->q_stride;
     const uint64_t dims[5] = {(uint64_t)s.D, (uint64_t)s.b, (uint64_t)s.M, (uint64_t)s.H,
                               (uint64_t)s.E};
-    const uint64_t str[4] = {(uint64_t)es[2] * 2, (uint64_t)es[2] * 2 * s.b, (uint64_t)es[1] * 2,
-                             (uint64_t)es[0] * 2};
-    ok = ok && encode(&tp.tm_qstr, dt, 5, p->q, dims, str, box_str);
+    const uint64_t str[4] = {(uint64_t)es[2] * esz, (uint64_t)es[2] * esz * s.b,
+                             (uint64_t)es[1] * esz, (uint64_t)es[0] * esz};
+    ok = ok && encode(&tp.tm_qstr, dt_in, 5, p->q, dims, str, box_str);
   }
   char* w = reinterpret_cast<char*>(p->workspace);
   const uint64_t rows = (uint64_t)slots * s.b * s.M;
@@ -221,7 +277,7 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
     const uint64_t sout[4] = {(uint64_t)os[2] * 2, (uint64_t)os[2] * 2 * s.b,
                               (uint64_t)os[1] * 2, (uint64_t)os[0] * 2};
     const uint32_t box5[5] = {64, 1, (uint32_t)s.M, 1, 1};
-    ok = ok && encode(&tp.tm_out_st, dt, 5, p->out, dout, sout, box5);
+    ok = ok && encode(&tp.tm_out_st, dt_out, 5, p->out, dout, sout, box5);
   }
   if (!ok) return cudaErrorInvalidValue;
   tp.al = w + ws.al;
@@ -233,6 +289,11 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   tp.ctrl = reinterpret_cast<uint32_t*>(w + ws.ctrl);
   tp.status = p->status;
   tp.status_host = p->status_host;
+  if (fp8) {
+    tp.qsc = p->q_scale;
+    tp.ksc = p->k_scale;
+    tp.vsc = p->v_scale;
+  }
   tp.stall_head = tp.stall_phase = -1;
   const char* stall = getenv("MA_TEST_STALL_DEP");  // "head,phase" (tests only)
   if (stall) {
@@ -285,7 +346,7 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   }
   const int64_t items = (int64_t)nheads * P * tiles;
   const int grid = (int)(items < sms ? items : sms);
-  err = dispatch(p->dtype == MA_DTYPE_BF16, s.b, s.M, s.D, tp, grid, st);
+  err = dispatch(p->dtype == MA_DTYPE_BF16, fp8, s.b, s.M, s.D, tp, grid, st);
   if (err == cudaSuccess) *nlaunch += 1;
   return err;
 }

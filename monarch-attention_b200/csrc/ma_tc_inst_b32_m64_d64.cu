@@ -5,9 +5,9 @@
 
 namespace ma {
 namespace tc {
-template cudaError_t launch_tc<true, 32, 64, 64, false>(const TcParams&, int, cudaStream_t);
-template cudaError_t launch_tc<true, 32, 64, 64, true>(const TcParams&, int, cudaStream_t);
-template cudaError_t launch_tc<false, 32, 64, 64, false>(const TcParams&, int, cudaStream_t);
-template cudaError_t launch_tc<false, 32, 64, 64, true>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<true, 32, 64, 64, false, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<true, 32, 64, 64, true, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 32, 64, 64, false, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 32, 64, 64, true, false>(const TcParams&, int, cudaStream_t);
 }  // namespace tc
 }  // namespace ma

@@ -5,9 +5,11 @@
 
 namespace ma {
 namespace tc {
-template cudaError_t launch_tc<true, 64, 64, 128, false>(const TcParams&, int, cudaStream_t);
-template cudaError_t launch_tc<true, 64, 64, 128, true>(const TcParams&, int, cudaStream_t);
-template cudaError_t launch_tc<false, 64, 64, 128, false>(const TcParams&, int, cudaStream_t);
-template cudaError_t launch_tc<false, 64, 64, 128, true>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<true, 64, 64, 128, false, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<true, 64, 64, 128, true, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 64, 64, 128, false, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 64, 64, 128, true, false>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 64, 64, 128, false, true>(const TcParams&, int, cudaStream_t);
+template cudaError_t launch_tc<false, 64, 64, 128, true, true>(const TcParams&, int, cudaStream_t);
 }  // namespace tc
 }  // namespace ma

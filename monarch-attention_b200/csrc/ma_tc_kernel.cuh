@@ -123,6 +123,11 @@ constexpr int kBarDrain = 160;   // MMA drain before the end
 constexpr int kBarStaged = 168;  // [kEntries] output tile(s) of the entry's tile staged (128)
 constexpr int kBarG2 = 192;      // [2] GEMM2 (all parts) of the group's tile issued
 constexpr int kBarDrain2 = 208;  // [2] MMAs a softmax group issued, complete (at the end)
+// e4m3 inputs (FP8 builds): the item's e4m3 tiles were converted in place to
+// f16 by its softmax group (128 arrivals; GEMM1 waits for it), and the late
+// V tile of a final R-step likewise (per group, before GEMM2's second part)
+constexpr int kBarConv = 224;    // [kEntries]
+constexpr int kBarVConv = 336;   // [2] (after the small objects at 320..327)
 
 // TMEM columns (fp32, 128 lanes): per group g, S/P at 256 g and O at 256 g + 128
 constexpr uint32_t kTmemCols = 512;
@@ -153,6 +158,10 @@ struct TcParams {
   uint4* clx;   // cl[j][k] as B_ext rows: (hi, lo) 16-bit pair padded to 16 bytes
   float* cr;
   const uint32_t* valid;  // validity bitmap [E][N / 32] (bit n % 32 of word n / 32), or null
+  // e4m3 inputs (FP8 builds): per-(e, h) dequantisation scales, x = x8 * s
+  const float* qsc;
+  const float* ksc;
+  const float* vsc;
   uint32_t* ctrl;
   uint32_t* status;
   uint32_t* status_host;  // host mirror of the status word (optional)
@@ -252,12 +261,48 @@ __device__ __forceinline__ uint32_t valid_word(const TcParams& p, int e, int tok
   return __ldg(p.valid + ((size_t)e * p.N + tok0) / 32);
 }
 
+// e4m3 -> f16 in place (FP8 builds): row `row` of a 128-row tile whose e4m3
+// values (128 per row, SW128: 16-byte unit c at position c ^ (row & 7)) were
+// loaded into its second 16 KB half; the f16 row (256 bytes) is written in
+// the tile's SW128 layout (half c / 4, units 2 (c % 4) and 2 (c % 4) + 1).
+// The row is read completely before anything is written, and no other
+// thread touches it, so converting in place is safe.  e4m3 values are exact
+// in f16.
+__device__ __forceinline__ void e4m3_row_to_f16(uint32_t tile, int row) {
+  const uint32_t src = tile + kHalf + row * 128;
+  uint32_t in[8][4];
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(in[c][0]), "=r"(in[c][1]), "=r"(in[c][2]), "=r"(in[c][3])
+                 : "r"(src + ((c ^ (row & 7)) << 4))
+                 : "memory");
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2_raw lo =
+          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[c][i] & 0xFFFFu), __NV_E4M3);
+      const __half2_raw hi =
+          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(in[c][i] >> 16), __NV_E4M3);
+      o[2 * i] = (uint32_t)lo.x | ((uint32_t)lo.y << 16);
+      o[2 * i + 1] = (uint32_t)hi.x | ((uint32_t)hi.y << 16);
+    }
+    const uint32_t dst = tile + (c >> 2) * kHalf + row * 128;
+    const int u = 2 * (c & 3);
+    st_shared_v4(dst + ((u ^ (row & 7)) << 4), o[0], o[1], o[2], o[3]);
+    st_shared_v4(dst + (((u + 1) ^ (row & 7)) << 4), o[4], o[5], o[6], o[7]);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
 // MASKED: the call has a validity bitmap (p.valid); the unmasked build
-// carries no mask code at all.
-template <bool BF16, int BB, int MM, int DD, bool MASKED>
+// carries no mask code at all.  FP8: q, k, v are e4m3 with per-head scales
+// (f16 tensor-core arithmetic, f16 intermediates, bf16 output).
+template <bool BF16, int BB, int MM, int DD, bool MASKED, bool FP8>
 __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constant__ TcParams p) {
   constexpr int PR = kT / BB;             // R items per tile
   constexpr int PL = kT / MM;             // L / output items per tile
@@ -269,6 +314,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
                 "block size and block count 32, 64 or 128");
   static_assert(DD == 64 || DD == 128, "head dim 64 or 128");
   static_assert(kTiles >= 1, "at least one tile per phase");
+  static_assert(!FP8 || (!BF16 && DD == 128), "e4m3 builds: f16 arithmetic, head dim 128");
+  constexpr int kInBytes = FP8 ? kHalf : kTileBytes;  // bytes of a q / k / v tile as loaded
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const uint32_t sbase = smem_u32(smem_raw);                       // small objects
   const uint32_t tbase = (sbase + kSmallBytes + 1023u) & ~1023u;   // SW128 tiles
@@ -301,6 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       mbar_init(bar(kBarCrTaken, g), 128);
     }
     for (int i = 0; i < kEntries; ++i) mbar_init(bar(kBarStaged, i), 128);
+    if (FP8) {
+      for (int i = 0; i < kEntries; ++i) mbar_init(bar(kBarConv, i), 128);
+      for (int g = 0; g < 2; ++g) mbar_init(bar(kBarVConv, g), 128);
+    }
     mbar_init(bar(kBarDrain, 0), 1);
     for (int g = 0; g < 2; ++g) {
       mbar_init(bar(kBarG2, g), 1);
@@ -428,7 +479,29 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         // the output phase, k before the final R-step); stream last uses and
         // the single-use intermediates
         const uint64_t keep = policy_evict_last(), once = policy_evict_first();
-        if (kind == KIND_R) {
+        if (FP8 && kind == KIND_R) {
+          // e4m3 q / k tiles (128 rows x 128 bytes) into the second half of
+          // their slot, converted to f16 in place by the softmax group
+          const bool first = ph == 0, final_ = ph == P - 2;
+          mbar_expect_tx(fb, (first ? kInBytes : kTileBytes) + kInBytes + (first ? 0 : 512));
+          if (!first) bulk_load(vdst, p.cr + vrow, 512, fb);
+          if (first)
+            tma_load_4d_h(A + kHalf, &p.tm_qblk, 0, tok0, hh, eb, fb, keep);
+          else
+            for (int h2 = 0; h2 < NH; ++h2)
+              tma_load_2d_h(A + h2 * kHalf, &p.tm_ar, h2 * 64, trow, fb, once);
+          tma_load_4d_h(B + kHalf, &p.tm_kblk, 0, tok0, hh, eb, fb, final_ ? once : keep);
+        } else if (FP8) {
+          mbar_expect_tx(fb, kInBytes + kTileBytes + kExtBytes);
+          bulk_load(vdst, p.clx + vrow, kExtBytes, fb);
+#pragma unroll
+          for (int pk = 0; pk < PL; ++pk)
+            tma_load_5d_h(A + kHalf + pk * MM * 128, &p.tm_qstr, 0, item * PL + pk, 0, hh, eb, fb,
+                          kind == KIND_O ? once : keep);
+#pragma unroll
+          for (int h2 = 0; h2 < NH; ++h2)
+            tma_load_2d_h(B + h2 * kHalf, &p.tm_al, h2 * 64, trow, fb, once);
+        } else if (kind == KIND_R) {
           const bool first = ph == 0, final_ = ph == P - 2;
           mbar_expect_tx(fb, 2 * kTileBytes + (first ? 0 : 512));
           if (!first) bulk_load(vdst, p.cr + vrow, 512, fb);
@@ -485,7 +558,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         ok = wait_bar(bar(kBarFull, e), (m / kEntries) & 1, guard);
         if (!ok) break;
         if (m >= *n_end_s) break;  // end marker: no tile m
-        if (m >= 2) ok = wait_bar(bar(kBarG2, gm), ((m - 2) >> 1) & 1, guard);
+        if (FP8) ok = wait_bar(bar(kBarConv, e), (m / kEntries) & 1, guard);  // e4m3 -> f16 done
+        if (ok && m >= 2) ok = wait_bar(bar(kBarG2, gm), ((m - 2) >> 1) & 1, guard);
         if (ok && prev_kind[gm] == KIND_L) {  // its cr lives in S[gm]: wait until read
           ok = wait_bar(bar(kBarCrTaken, gm), cr_waits[gm] & 1, guard);
           ++cr_waits[gm];
@@ -534,9 +608,43 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
     constexpr uint32_t id_mm = idesc_f16(BF16, true, true, 128, DD);   // ar = P^T Q_j
     constexpr uint32_t id_cr = idesc_f16(BF16, true, false, 128, 16);  // cr = P^T 1
     uint32_t g2_parts = 0;  // O parts this group committed (row 0)
+    uint32_t vconv = 0;     // final R-step V tiles this group converted (FP8)
     for (uint32_t k = 0;; ++k) {
       const uint32_t n = 2 * k + g;
       const int e = n % kEntries;
+      if (FP8) {
+        // convert this tile's e4m3 operands to f16 (row `row` of each) as
+        // soon as they land; GEMM1 waits for the 128 arrivals.  The wait also
+        // watches the end marker: after the last tile the producer posts it on
+        // one entry only, and the tile this group waits for may not exist.
+        bool ready = false;
+        {
+          const uint32_t fb = bar(kBarFull, e), par = (n / kEntries) & 1;
+          const uint64_t t0 = globaltimer();
+          for (uint32_t spin = 0;; ++spin) {
+            if (mbar_try(fb, par)) {
+              ready = true;
+              break;
+            }
+            if (n >= *n_end_s) break;  // no such tile
+            if ((spin & 63u) == 0) {
+              if (ld_relaxed(guard.abort)) break;
+              if (globaltimer() - t0 > guard.limit) {
+                guard.raise(MA_STATUS_WAIT_TIMEOUT);
+                break;
+              }
+            }
+          }
+        }
+        if (!__all_sync(0xffffffffu, ready)) break;
+        if (n >= *n_end_s) break;
+        const int4 dc = desc_slot[e];
+        const uint32_t At = tbase + e * kEntryBytes, Bt = At + kTileBytes;
+        if (dc.w != KIND_R || dc.y == 0) e4m3_row_to_f16(At, row);  // q blocks / Q_j
+        if (dc.w == KIND_R) e4m3_row_to_f16(Bt, row);               // k blocks
+        fence_proxy_async_smem();
+        mbar_arrive(bar(kBarConv, e));
+      }
       if (!wait_bar_warp(bar(kBarSFull, g), k & 1, guard)) break;
       if (n >= *n_end_s) break;
       // the entry's vector was written by the async proxy: observe its
@@ -567,13 +675,18 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         fence_proxy_async_global();
         const uint32_t xb = bar(kBarX, e);
         const uint64_t once = policy_evict_first();  // V and y_j: single use
-        mbar_expect_tx(xb, kTileBytes);
+        if (FP8 && final_) {  // e4m3 V (converted before GEMM2's second part)
+          mbar_expect_tx(xb, kInBytes);
+          tma_load_4d_h(A + kHalf, &p.tm_vblk, 0, item * kT, hh, eb, xb, once);
+        } else {
+          mbar_expect_tx(xb, kTileBytes);
 #pragma unroll
-        for (int h2 = 0; h2 < NH; ++h2) {
-          if (final_)
-            tma_load_4d_h(A + h2 * kHalf, &p.tm_vblk, h2 * 64, item * kT, hh, eb, xb, once);
-          else
-            tma_load_2d_h(A + h2 * kHalf, &p.tm_y, h2 * 64, trow, xb, once);
+          for (int h2 = 0; h2 < NH; ++h2) {
+            if (final_)
+              tma_load_4d_h(A + h2 * kHalf, &p.tm_vblk, h2 * 64, item * kT, hh, eb, xb, once);
+            else
+              tma_load_2d_h(A + h2 * kHalf, &p.tm_y, h2 * 64, trow, xb, once);
+          }
         }
       }
 
@@ -611,6 +724,14 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       // memory.  Everything outside the block is written as zero.
       float c = 1.0f;  // R: sm_scale / (cr_j + eps)
       if (rk) c = p.sm_scale / ((ph > 0 ? vec[row] : 1.0f) + kEps);
+      // e4m3: S was computed on the unscaled values: R logits carry s_k
+      // (and s_q in round 0), L / output logits were computed as
+      // (q8 al^T - cl / s_q) and are s_q times that
+      float sq = 1.0f;
+      if (FP8) {
+        sq = __ldg(p.qsc + head);
+        if (rk) c *= __ldg(p.ksc + head) * (ph == 0 ? sq : 1.0f);
+      }
       uint32_t ca[32], cb[32];
       float mx;
       {
@@ -649,6 +770,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       } else {
         u_a = kLog2e;  // x = S - cl[k] (subtracted by GEMM1)
         u_b = -mx * kLog2e;
+        if (FP8) {
+          u_a *= sq;
+          u_b *= sq;
+        }
       }
       float s4[4] = {0.f, 0.f, 0.f, 0.f}, w4[4] = {0.f, 0.f, 0.f, 0.f};
       uint64_t s2[2] = {0ull, 0ull}, w2[2] = {0ull, 0ull};
@@ -725,7 +850,8 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         // as the B_ext row of the later GEMM that subtracts it: cl split into
         // a 16-bit value and the 16-bit rounding of the remainder (their sum
         // carries ~16 significant bits)
-        const float clv = kLn2 * inv * wsum - __logf(den) * sum * inv;
+        float clv = kLn2 * inv * wsum - __logf(den) * sum * inv;
+        if (FP8) clv /= sq;  // subtracted from q8 al^T (the unscaled logits)
         const float hi = round16<BF16>(clv);
         p.clx[(size_t)(slot * BB + row % BB) * MM + kblock] =
             make_uint4(pack2<BF16>(hi, clv - hi), 0u, 0u, 0u);
@@ -778,40 +904,62 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       tc_fence_before();
       mbar_arrive(bar(kBarPReady, g));
       if (row == 0) trace_stamp(p, n, 5, globaltimer());
-      if (row == 0) {
-        // GEMM2 of this tile, issued here as soon as its P (all 128 rows),
-        // its late X tile and the group's O accumulator are ready; then the
-        // MMA warp may reuse S of the group (kBarG2)
-        bool ok2 = wait_bar(bar(kBarPReady, g), k & 1, guard);
-        const int nparts = final_ ? 2 : 1;
-        for (int part = 0; ok2 && part < nparts; ++part) {
-          if (kind == KIND_O || part == 1) ok2 = wait_bar(bar(kBarX, e), (n / kEntries) & 1, guard);
-          if (ok2 && g2_parts > 0) ok2 = wait_bar(bar(kBarOFree, g), (g2_parts - 1) & 1, guard);
-          if (!ok2) break;
-          tc_fence_after();
-          const uint32_t tSg = tmem + 256 * g, tO = tSg + 128;
-          if (kind == KIND_L) {
+      // GEMM2 of this tile, issued by the group's thread 0 as soon as its P
+      // (all 128 rows), its late X tile and the group's O accumulator are
+      // ready; then the MMA warp may reuse S of the group (kBarG2)
+      auto issue_part = [&](int part) -> bool {
+        bool ok = true;
+        if (kind == KIND_O || part == 1) ok = wait_bar(bar(kBarX, e), (n / kEntries) & 1, guard);
+        if (FP8 && ok && part == 1) ok = wait_bar(bar(kBarVConv, g), vconv & 1, guard);
+        if (ok && g2_parts > 0) ok = wait_bar(bar(kBarOFree, g), (g2_parts - 1) & 1, guard);
+        if (!ok) return false;
+        tc_fence_after();
+        const uint32_t tSg = tmem + 256 * g, tO = tSg + 128;
+        if (kind == KIND_L) {
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t pd = smem_desc(B + kk * 2048, kHalf, 1024, kSwz128);  // P^T
-              mma_ss(tO, pd, smem_desc(A + kk * 2048, kHalf, 1024, kSwz128), id_mm, kk > 0);
-              mma_ss(tSg, pd, smem_desc(sbase + kOffOnes, 128, 256, kSwzNone), id_cr, kk > 0);
-            }
-          } else if (kind == KIND_O || part == 1) {
-            gemm2_ts<BF16, DD>(tO, tSg, A);  // out: P y_j; R-final part 2: P V[m] (tile A)
-          } else {
-            gemm2_ts<BF16, DD>(tO, tSg, B);  // R: P K[m]
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t pd = smem_desc(B + kk * 2048, kHalf, 1024, kSwz128);  // P^T
+            mma_ss(tO, pd, smem_desc(A + kk * 2048, kHalf, 1024, kSwz128), id_mm, kk > 0);
+            mma_ss(tSg, pd, smem_desc(sbase + kOffOnes, 128, 256, kSwzNone), id_cr, kk > 0);
           }
-          mma_commit(bar(kBarOFull, g));
-          ++g2_parts;
+        } else if (kind == KIND_O || part == 1) {
+          gemm2_ts<BF16, DD>(tO, tSg, A);  // out: P y_j; R-final part 2: P V[m] (tile A)
+        } else {
+          gemm2_ts<BF16, DD>(tO, tSg, B);  // R: P K[m]
         }
-        // (a failed wait leaves through the abort flag at the group's next
-        // warp-uniform wait, so the warp's lanes stay together)
-        if (ok2) {
-          tc_fence_before();
-          mbar_arrive(bar(kBarG2, g));
-        }
+        mma_commit(bar(kBarOFull, g));
+        ++g2_parts;
+        return true;
+      };
+      // e4m3 final R-step: the late V tile -> f16 before GEMM2's second part;
+      // warps 1-3 of the group convert their rows right away, warp 0 once its
+      // thread 0 has issued the first part (P K[m], which does not read V)
+      const bool vconv_now = FP8 && final_;
+      auto convert_v = [&]() -> bool {
+        if (!wait_bar_warp(bar(kBarX, e), (n / kEntries) & 1, guard)) return false;
+        e4m3_row_to_f16(A, row);
+        fence_proxy_async_smem();
+        mbar_arrive(bar(kBarVConv, g));
+        return true;
+      };
+      if (vconv_now && (warp & 3) != 0 && !convert_v()) break;
+      // (a failed wait leaves through the abort flag at the group's next
+      // warp-uniform wait, so the warp's lanes stay together)
+      bool ok2 = true;
+      if (row == 0) {
+        ok2 = wait_bar(bar(kBarPReady, g), k & 1, guard);
+        const int nparts = vconv_now ? 1 : (final_ ? 2 : 1);
+        for (int part = 0; ok2 && part < nparts; ++part) ok2 = issue_part(part);
       }
+      if (vconv_now && (warp & 3) == 0) {
+        if (!convert_v()) break;
+        if (row == 0 && ok2) ok2 = issue_part(1);
+      }
+      if (row == 0 && ok2) {
+        tc_fence_before();
+        mbar_arrive(bar(kBarG2, g));
+      }
+      if (FP8 && final_) ++vconv;
     }
     if (row == 0) {
       // The epilogue may still be draining this group's last tile: post the
@@ -854,10 +1002,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       const float scale_out = scale_ring[(n % kScaleRing) * 128 + row];
       const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
       const bool final_ = kind == KIND_R && ph == P - 2;
+      // e4m3: the GEMM2 operands k, v, q_j were unscaled
+      const float s_k = FP8 ? __ldg(p.ksc + head) : 1.0f;
       if (kind == KIND_R) {
         // al[j][m] = sm_scale * r K[m] (ma_torch.py:21); R-final stages it in
         // tile B (K is consumed) while its second GEMM2 part reads V in tile A
-        stage_row<BF16, NH>(final_ ? B : A, row, tO, p.sm_scale * scale_out);
+        stage_row<BF16, NH>(final_ ? B : A, row, tO, p.sm_scale * scale_out * s_k);
         if (final_) {
           // y[j][m] = r V[m] (:51), second pass through O
           tc_fence_before();
@@ -865,7 +1015,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           if (!wait_bar_warp(bar(kBarOFull, g), eparts[g] & 1, guard)) break;
           tc_fence_after();
           ++eparts[g];
-          stage_row<BF16, NH>(A, row, tO, scale_out);
+          stage_row<BF16, NH>(A, row, tO, scale_out * (FP8 ? __ldg(p.vsc + head) : 1.0f));
         }
       } else if (kind == KIND_L) {
         // cr[k][j] = sum_l P[l][k] (the N = 16 GEMM into S[g]; read it first,
@@ -878,10 +1028,10 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         // cr[k][j] of this row: k = row % M, j = the row's index
         p.cr[(size_t)(slot * MM + row % MM) * BB + item * PL + row / MM] = __uint_as_float(o[0]);
         // ar[k][j] = sum_l P[l][k] q[l*b+j] (:34)
-        stage_row<BF16, NH>(A, row, tO, 1.0f);
+        stage_row<BF16, NH>(A, row, tO, FP8 ? __ldg(p.qsc + head) : 1.0f);
       } else {
-        // z[l*b + j] = (P y_j) / sum (ma_torch.py:60-62)
-        stage_row<BF16, NH>(A, row, tO, scale_out);
+        // z[l*b + j] = (P y_j) / sum (ma_torch.py:60-62); e4m3 calls return bf16
+        stage_row<(BF16 || FP8), NH>(A, row, tO, scale_out);
         // y_j has no other reader: drop it from L2 (GEMM2 consumed it)
         const char* ytile = p.y + ((size_t)slot * BB * MM + item * kT) * DD * 2;
 #pragma unroll
@@ -974,9 +1124,9 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
 }
 
 // Launch one forward on `grid` persistent CTAs (grid <= SM count).
-template <bool BF16, int BB, int MM, int DD, bool MASKED>
+template <bool BF16, int BB, int MM, int DD, bool MASKED, bool FP8>
 cudaError_t launch_tc(const TcParams& tp, int grid, cudaStream_t st) {
-  auto kfn = ma_tc_kernel<BF16, BB, MM, DD, MASKED>;
+  auto kfn = ma_tc_kernel<BF16, BB, MM, DD, MASKED, FP8>;
   cudaError_t err =
       cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(DD));
   if (err != cudaSuccess) return err;

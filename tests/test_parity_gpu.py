@@ -453,7 +453,8 @@ def test_e4m3_against_dequantised_oracle(name, shape, impl, cuda_device):
 
 
 def test_e4m3_routes_to_tensor_core_kernels(cuda_device):
-    """e4m3 inputs run on the tensor-core kernels after a bf16 conversion."""
+    """e4m3 inputs run on the tensor-core kernels (directly, or after a bf16
+    conversion for the shapes the e4m3 build does not take)."""
     for name, shape, want in [("long16k_e4m3", dict(E=1, H=1), "tc"),
                               ("long4k_bf16", dict(E=1, H=1), "tc"),
                               ("long64k_bf16", dict(E=1, H=1), "tc"),
@@ -464,8 +465,33 @@ def test_e4m3_routes_to_tensor_core_kernels(cuda_device):
         assert mab.selected_impl(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad) == want, name
 
 
+@pytest.mark.parametrize("name,shape", [("long16k_e4m3", dict(E=1, H=3)),
+                                        ("long4k_e4m3", dict(E=2, H=3)),
+                                        ("long4k_e4m3", dict(E=2, H=2, mask_min_len=1500))])
+def test_e4m3_direct_matches_conversion_route(name, shape, cuda_device, monkeypatch):
+    """The persistent kernel reads e4m3 tiles itself (converted to f16 in
+    shared memory, scales folded into the softmax and epilogue); the result
+    agrees with the route through bf16 copies and with the oracle."""
+    cfg = CONFIGS[name].with_(**shape)
+    q, k, v, mask, scales = make_inputs(cfg, device=cuda_device)
+    direct = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, scales=scales)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    monkeypatch.setenv("MA_FP8_CONVERT", "1")
+    conv = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, scales=scales)
+    torch.cuda.synchronize()
+    check_status(cuda_device)
+    assert direct.dtype == torch.bfloat16 and torch.isfinite(direct.float()).all()
+    scale = float(conv.float().abs().max())
+    assert float((direct.float() - conv.float()).abs().max()) <= 3e-2 * scale
+    deq = [dequantize_e4m3(t, s_).cpu() for t, s_ in zip((q, k, v), scales)]
+    ref = oracle_for(*deq, None if mask is None else mask.cpu(), cfg, "f32")
+    err = np.abs(direct.float().cpu().numpy() - ref).max()
+    assert err <= E4M3_TOL * float(np.abs(ref).max()), f"max|err|={err:.3g}"
+
+
 def test_e4m3_full_size_tc(cuda_device):
-    """long16k e4m3 at full size through the conversion + tcgen05 route."""
+    """long16k e4m3 at full size on the persistent kernel (e4m3 read directly)."""
     cfg = CONFIGS["long16k_e4m3"]
     q, k, v, mask, scales = make_inputs(cfg, device=cuda_device)
     out = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, scales=scales)
