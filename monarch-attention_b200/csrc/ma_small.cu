@@ -592,6 +592,9 @@ static cudaError_t launch(const SmallParams& sp, cudaStream_t st) {
 
 // ma_small_f32.cu: the same fused kernel in fp32 (FFMA)
 bool small_f32_supports(const ma_fwd_params* p, const Shape& s);
+// ma_small_res.cu: the head-resident variant (intermediates in shared memory)
+bool small_res_supports(const ma_fwd_params* p, const Shape& s);
+cudaError_t run_small_res(const ma_fwd_params* p, const Shape& s, cudaStream_t st, int* nlaunch);
 cudaError_t run_small_f32(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
                           cudaStream_t st, int* nlaunch);
 
@@ -618,6 +621,7 @@ bool small_supports(const ma_fwd_params* p, const Shape& s) {
 cudaError_t run_small(const ma_fwd_params* p, const Shape& s, const WsLayout& ws,
                       cudaStream_t st, int* nlaunch) {
   if (p->dtype == MA_DTYPE_F32) return run_small_f32(p, s, ws, st, nlaunch);
+  if (small_res_supports(p, s)) return run_small_res(p, s, st, nlaunch);
   small::SmallParams sp{};
   sp.q = p->q; sp.k = p->k; sp.v = p->v; sp.out = p->out;
   for (int i = 0; i < 4; ++i) {

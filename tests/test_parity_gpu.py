@@ -179,8 +179,10 @@ def test_caller_layout_in_and_out(impl, shape, cuda_device):
 def test_small_kernel_cluster_sizes(csize, dtype, cuda_device, monkeypatch):
     """The small-block kernels (mma.sync 16-bit, FFMA fp32) split a head over a
     cluster of 1, 2 or 4 CTAs; every split gives the oracle's result (masked
-    RoBERTa shape, T = 3)."""
+    RoBERTa shape, T = 3).  The head-resident kernel, which takes this shape
+    in 16 bits, is switched off so the workspace kernel runs."""
     monkeypatch.setenv("MA_SMALL_CLUSTER", csize)
+    monkeypatch.setenv("MA_DISABLE_SMALL_RES", "1")
     cfg = CONFIGS["roberta_bf16"].with_(E=2, H=2, T=3, dtype=dtype)
     q, k, v, mask, _ = make_inputs(cfg, device="cpu")
     out = monarch_attention(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device),
