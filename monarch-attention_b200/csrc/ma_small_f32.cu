@@ -376,13 +376,11 @@ __global__ void __launch_bounds__(kThreads, 1) ma_small_f32_kernel(const Params 
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
   // token validity of the padded sequence (pad positions and the mask row)
   const int Np = p.M * p.b;
-  for (int w = threadIdx.x; w < (TL::kMaxTokens + 31) / 32; w += kThreads) {
-    uint32_t bits = 0;
-    for (int i = 0; i < 32; ++i) {
-      const int pidx = w * 32 + i;
-      if (pidx < Np && token_valid(p, e, pidx)) bits |= 1u << i;
-    }
-    vbits[w] = bits;
+  // (one lane per token, so the mask loads of a word are issued together)
+  for (int w = warp; w < (TL::kMaxTokens + 31) / 32; w += kWarps) {
+    const int pidx = w * 32 + lane;
+    const uint32_t bits = __ballot_sync(0xffffffffu, pidx < Np && token_valid(p, e, pidx));
+    if (lane == 0) vbits[w] = bits;
   }
   __syncthreads();
   for (int t = 0; t < p.T; ++t) {

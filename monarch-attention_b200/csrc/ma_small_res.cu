@@ -43,7 +43,22 @@ struct Params {
   int mask_dtype;
   int E, H, N, b, M, T, pad_off;
   float sm_scale;
+  unsigned long long* trace;  // MA_SMALL_TRACE builds: per-head phase timestamps, else null
 };
+
+// Optional per-head timeline (compiled in with -DMA_SMALL_TRACE): slot 0 the
+// start, slot 1 the bitmap built, slot 2 + i the end of phase i (16 slots).
+__device__ __forceinline__ void trace_stamp(const Params& p, int head, int slot) {
+#ifdef MA_SMALL_TRACE
+  if (p.trace != nullptr && threadIdx.x == 0 && slot < 16) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    p.trace[(size_t)head * 16 + slot] = t;
+  }
+#else
+  (void)p; (void)head; (void)slot;
+#endif
+}
 
 enum { PH_R = 0, PH_RF = 1, PH_L = 2, PH_O = 3 };
 
@@ -122,11 +137,17 @@ struct View {
   }
 };
 
+// Offset of the validity bitmap: behind al, ary (b M rows each) and cl, cr
+// (b M floats each), rounded up to 128 bytes so that the staging tiles
+// behind it stay 16-byte aligned for cp.async and ldmatrix whatever b M is.
+__host__ __device__ constexpr size_t bits_offset(int np, int row_bytes) {
+  return ((size_t)2 * np * row_bytes + (size_t)2 * np * 4 + 127) / 128 * 128;
+}
+
 // bytes of shared memory for a head of b x M items, tiles of RT rows
 template <int DP>
 __host__ __device__ constexpr size_t smem_bytes(int b, int M, int RT) {
-  return (size_t)2 * b * M * (DP * 2)   // al, ary
-         + (size_t)2 * b * M * 4        // cl, cr
+  return bits_offset(b * M, DP * 2)     // al, ary, cl, cr
          + 128                          // validity bitmap (<= 1024 tokens)
          + (size_t)kWarps * 2 * RT * (DP * 2);  // staging tiles T0, T1 per warp
 }
@@ -174,7 +195,7 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, ui
   const uint32_t s_ary = s_al + (uint32_t)(b * M * RBY);
   float* cl = reinterpret_cast<float*>(sm + 2 * (size_t)b * M * RBY);
   float* cr = cl + b * M;
-  const uint32_t* vbits = reinterpret_cast<const uint32_t*>(cr + b * M);
+  const uint32_t* vbits = reinterpret_cast<const uint32_t*>(sm + bits_offset(b * M, RBY));
   const View T0{t0s, RBY, 0}, T1{t1s, RBY, 0};
   const size_t esz = sizeof(TI);
   const char* qh = reinterpret_cast<const char*>(p.q) + esz * (e * p.qs[0] + h * p.qs[1]);
@@ -486,22 +507,22 @@ __global__ void __launch_bounds__(kThreads, (RB == 16 && RM == 16) ? 2 : 1)
   const int eh = blockIdx.x;
   const int e = eh / p.H, h = eh - e * p.H;
   const int b = p.b, M = p.M;
-  const size_t res = (size_t)2 * b * M * (DP * 2) + (size_t)2 * b * M * 4;
+  const size_t res = bits_offset(b * M, DP * 2);
   uint32_t* vbits = reinterpret_cast<uint32_t*>(sm + res);
   uint8_t* tiles = sm + res + 128;
   const uint32_t t0s = smem_u32(tiles + (size_t)warp * 2 * RT * (DP * 2));
   const uint32_t t1s = t0s + RT * (DP * 2);
+  trace_stamp(p, eh, 0);
   // token validity of the padded sequence (pad positions and the mask row)
+  // (one lane per token, so the mask loads of a word are issued together)
   const int Np = M * b;
-  for (int w = threadIdx.x; w < (Np + 31) / 32; w += kThreads) {
-    uint32_t bits = 0;
-    for (int i = 0; i < 32; ++i) {
-      const int pidx = w * 32 + i;
-      if (pidx < Np && token_valid(p, e, pidx)) bits |= 1u << i;
-    }
-    vbits[w] = bits;
+  for (int w = warp; w < (Np + 31) / 32; w += kWarps) {
+    const int pidx = w * 32 + lane;
+    const uint32_t bits = __ballot_sync(0xffffffffu, pidx < Np && token_valid(p, e, pidx));
+    if (lane == 0) vbits[w] = bits;
   }
   __syncthreads();
+  trace_stamp(p, eh, 1);
   for (int t = 0; t < p.T; ++t) {
     const bool final_ = t == p.T - 1;
     for (int m = warp; m < M; m += kWarps) {
@@ -511,6 +532,7 @@ __global__ void __launch_bounds__(kThreads, (RB == 16 && RM == 16) ? 2 : 1)
         run_item<PH_R, BF16, DP, RB, RM>(p, e, h, m, t == 0, sm, t0s, t1s, lane);
     }
     __syncthreads();
+    trace_stamp(p, eh, 2 + 2 * t);
     for (int j = warp; j < b; j += kWarps) {
       if (final_)
         run_item<PH_O, BF16, DP, RB, RM>(p, e, h, j, false, sm, t0s, t1s, lane);
@@ -518,6 +540,7 @@ __global__ void __launch_bounds__(kThreads, (RB == 16 && RM == 16) ? 2 : 1)
         run_item<PH_L, BF16, DP, RB, RM>(p, e, h, j, false, sm, t0s, t1s, lane);
     }
     __syncthreads();
+    trace_stamp(p, eh, 3 + 2 * t);
   }
 }
 
@@ -581,6 +604,10 @@ cudaError_t run_small_res(const ma_fwd_params* p, const Shape& s, cudaStream_t s
   sp.mask_dtype = p->mask_dtype;
   sp.E = s.E; sp.H = s.H; sp.N = s.N; sp.b = s.b; sp.M = s.M; sp.T = s.T;
   sp.pad_off = s.pad_off; sp.sm_scale = s.sm_scale;
+#ifdef MA_SMALL_TRACE
+  const char* trc = getenv("MA_SMALL_TRACE_PTR");  // device buffer of E*H x 16 u64
+  if (trc) sp.trace = reinterpret_cast<unsigned long long*>(strtoull(trc, nullptr, 0));
+#endif
   const bool bf = p->dtype == MA_DTYPE_BF16;
   const int rb = smallr::round16(s.b), rm = smallr::round16(s.M);
   cudaError_t err = cudaErrorInvalidValue;
