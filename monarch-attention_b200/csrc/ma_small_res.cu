@@ -175,12 +175,36 @@ __device__ __forceinline__ void stage(const View& dst, const char* base, int64_t
   }
 }
 
+// Issue (no wait) the cp.async copies of the q / k / v rows an item reads:
+// R-steps k[m] -> T1, the first round's q[m] -> T0, the final R-step's v[m]
+// -> T0 (after round 0; a single-round call stages v inside the item, once
+// GEMM1 has read q); L / output steps Q_j -> T0.  q, k and v are inputs, so
+// a warp may stage its next item while other warps finish the current phase.
+template <int PH, int DP, int RB, int RM>
+__device__ __forceinline__ void stage_item(const Params& p, int e, int h, int item, bool first,
+                                           uint32_t t0s, uint32_t t1s, int lane) {
+  constexpr int RBY = DP * 2;
+  const View T0{t0s, RBY, 0}, T1{t1s, RBY, 0};
+  const char* qh = reinterpret_cast<const char*>(p.q) + 2 * (e * p.qs[0] + h * p.qs[1]);
+  if (PH == PH_R || PH == PH_RF) {
+    const char* kh = reinterpret_cast<const char*>(p.k) + 2 * (e * p.ks[0] + h * p.ks[1]);
+    if (first) stage<DP, RB>(T0, qh, 2 * p.qs[2], p, item * p.b, 1, p.b, lane);
+    stage<DP, RB>(T1, kh, 2 * p.ks[2], p, item * p.b, 1, p.b, lane);
+    if (PH == PH_RF && !first) {
+      const char* vh = reinterpret_cast<const char*>(p.v) + 2 * (e * p.vs[0] + h * p.vs[1]);
+      stage<DP, RB>(T0, vh, 2 * p.vs[2], p, item * p.b, 1, p.b, lane);
+    }
+  } else {
+    stage<DP, RM>(T0, qh, 2 * p.qs[2], p, item, p.b, p.M, lane);
+  }
+}
+
 // One work item, executed by one warp.  R / RF: key block m (RB x RB logits:
 // rows j, columns i of block m).  L / O: index j (RM x RM logits: rows l,
 // columns k).  Rows and columns beyond b (R) or M (L / O) are padding.
 template <int PH, bool BF16, int DP, int RB, int RM>
-__device__ void run_item(const Params& p, int e, int h, int item, bool first, uint8_t* sm,
-                         uint32_t t0s, uint32_t t1s, int lane) {
+__device__ void run_item(const Params& p, int e, int h, int item, bool first, bool staged,
+                         uint8_t* sm, uint32_t t0s, uint32_t t1s, int lane) {
   constexpr bool kR = PH == PH_R || PH == PH_RF;
   constexpr int ROWS = kR ? RB : RM;
   constexpr int MT = ROWS / 16;  // m16 tiles
@@ -198,29 +222,21 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, ui
   const uint32_t* vbits = reinterpret_cast<const uint32_t*>(sm + bits_offset(b * M, RBY));
   const View T0{t0s, RBY, 0}, T1{t1s, RBY, 0};
   const size_t esz = sizeof(TI);
-  const char* qh = reinterpret_cast<const char*>(p.q) + esz * (e * p.qs[0] + h * p.qs[1]);
-  const char* kh = reinterpret_cast<const char*>(p.k) + esz * (e * p.ks[0] + h * p.ks[1]);
   const char* vh = reinterpret_cast<const char*>(p.v) + esz * (e * p.vs[0] + h * p.vs[1]);
 
-  // ---- operand views and staging ----
+  // ---- operand views (staged rows: stage_item, here or ahead) ----
+  if (!staged) stage_item<PH, DP, RB, RM>(p, e, h, item, first, t0s, t1s, lane);
   View A, B, X1, X2;
   if (kR) {
     // A: q block m (first round) or ar[m][.] (resident); B, X1: k block m;
     // X2: v block m (final R-step)
-    if (first) {
-      stage<DP, RB>(T0, qh, esz * p.qs[2], p, item * b, 1, b, lane);
-      A = T0;
-    } else {
-      A = View{s_ary + (uint32_t)(item * b * RBY), RBY, item};
-    }
-    stage<DP, RB>(T1, kh, esz * p.ks[2], p, item * b, 1, b, lane);
+    A = first ? T0 : View{s_ary + (uint32_t)(item * b * RBY), RBY, item};
     B = T1;
     X1 = T1;
-    X2 = T0;  // final R-step: V[m] (staged once T0 is free)
+    X2 = T0;
   } else {
     // A: Q_j = tokens l * b + j; B: al[j][.] (resident); X1 (output step):
     // y[.][j] (resident rows m * b + j)
-    stage<DP, RM>(T0, qh, esz * p.qs[2], p, item, b, M, lane);
     A = T0;
     B = View{s_al + (uint32_t)(item * M * RBY), RBY, item};
     X1 = View{s_ary + (uint32_t)(item * RBY), (uint32_t)(b * RBY), item};
@@ -253,13 +269,7 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, ui
   // the final R-step's V goes into T0: at once when A is resident; in a
   // single-round call (T = 1, A = q in T0) after GEMM1, which then has one
   // row tile only (b <= 16, see small_res_supports)
-  bool v_staged = false;
-  if (PH == PH_RF && !first) {
-    stage<DP, RB>(T0, vh, esz * p.vs[2], p, item * b, 1, b, lane);
-    cp_async_wait_all();
-    __syncwarp();
-    v_staged = true;
-  }
+  bool v_staged = PH == PH_RF && !first;
   const int rlast = R - 1;
 
 #pragma unroll 1
@@ -523,21 +533,53 @@ __global__ void __launch_bounds__(kThreads, (RB == 16 && RM == 16) ? 2 : 1)
   }
   __syncthreads();
   trace_stamp(p, eh, 1);
+  // Each warp stages the q / k / v rows of its next item as soon as the
+  // current one is done -- across phase barriers too (they are inputs) -- so
+  // an item waits only for copies issued an item earlier.
+  if (warp < M)
+    stage_item<PH_R, DP, RB, RM>(p, e, h, warp, true, t0s, t1s, lane);  // same rows as RF
   for (int t = 0; t < p.T; ++t) {
     const bool final_ = t == p.T - 1;
     for (int m = warp; m < M; m += kWarps) {
       if (final_)
-        run_item<PH_RF, BF16, DP, RB, RM>(p, e, h, m, t == 0, sm, t0s, t1s, lane);
+        run_item<PH_RF, BF16, DP, RB, RM>(p, e, h, m, t == 0, true, sm, t0s, t1s, lane);
       else
-        run_item<PH_R, BF16, DP, RB, RM>(p, e, h, m, t == 0, sm, t0s, t1s, lane);
+        run_item<PH_R, BF16, DP, RB, RM>(p, e, h, m, t == 0, true, sm, t0s, t1s, lane);
+      // next: this phase's next R item, else this warp's first L / output item
+      if (m + kWarps < M) {
+        if (final_)
+          stage_item<PH_RF, DP, RB, RM>(p, e, h, m + kWarps, t == 0, t0s, t1s, lane);
+        else
+          stage_item<PH_R, DP, RB, RM>(p, e, h, m + kWarps, t == 0, t0s, t1s, lane);
+      } else if (warp < b) {
+        stage_item<PH_L, DP, RB, RM>(p, e, h, warp, false, t0s, t1s, lane);  // = output rows
+      }
     }
+    if (warp >= M && warp < b)
+      stage_item<PH_L, DP, RB, RM>(p, e, h, warp, false, t0s, t1s, lane);
     __syncthreads();
     trace_stamp(p, eh, 2 + 2 * t);
+    const bool next_final = t + 1 == p.T - 1;
     for (int j = warp; j < b; j += kWarps) {
       if (final_)
-        run_item<PH_O, BF16, DP, RB, RM>(p, e, h, j, false, sm, t0s, t1s, lane);
+        run_item<PH_O, BF16, DP, RB, RM>(p, e, h, j, false, true, sm, t0s, t1s, lane);
       else
-        run_item<PH_L, BF16, DP, RB, RM>(p, e, h, j, false, sm, t0s, t1s, lane);
+        run_item<PH_L, BF16, DP, RB, RM>(p, e, h, j, false, true, sm, t0s, t1s, lane);
+      // next: this phase's next item, else the next round's first R item
+      if (j + kWarps < b) {
+        stage_item<PH_L, DP, RB, RM>(p, e, h, j + kWarps, false, t0s, t1s, lane);
+      } else if (!final_ && warp < M) {
+        if (next_final)
+          stage_item<PH_RF, DP, RB, RM>(p, e, h, warp, false, t0s, t1s, lane);
+        else
+          stage_item<PH_R, DP, RB, RM>(p, e, h, warp, false, t0s, t1s, lane);
+      }
+    }
+    if (!final_ && warp >= b && warp < M) {
+      if (next_final)
+        stage_item<PH_RF, DP, RB, RM>(p, e, h, warp, false, t0s, t1s, lane);
+      else
+        stage_item<PH_R, DP, RB, RM>(p, e, h, warp, false, t0s, t1s, lane);
     }
     __syncthreads();
     trace_stamp(p, eh, 3 + 2 * t);
