@@ -1002,36 +1002,52 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       const float scale_out = scale_ring[(n % kScaleRing) * 128 + row];
       const uint32_t A = tbase + e * kEntryBytes, B = A + kTileBytes;
       const bool final_ = kind == KIND_R && ph == P - 2;
-      // e4m3: the GEMM2 operands k, v, q_j were unscaled
-      const float s_k = FP8 ? __ldg(p.ksc + head) : 1.0f;
-      if (kind == KIND_R) {
-        // al[j][m] = sm_scale * r K[m] (ma_torch.py:21); R-final stages it in
-        // tile B (K is consumed) while its second GEMM2 part reads V in tile A
-        stage_row<BF16, NH>(final_ ? B : A, row, tO, p.sm_scale * scale_out * s_k);
-        if (final_) {
-          // y[j][m] = r V[m] (:51), second pass through O
+      // One staging call site for every output (the kernel's speed follows
+      // its code size): R tiles al[j][m] = sm_scale * r K[m] (ma_torch.py:21),
+      // staged in tile B for R-final tiles (K is consumed) while their second
+      // GEMM2 part reads V in tile A, then y[j][m] = r V[m] (:51) from a second
+      // pass through O; L tiles ar[k][j] = sum_l P[l][k] q[l*b+j] (:34); output
+      // tiles z[l*b + j] = (P y_j) / sum (:60-62).  e4m3: the GEMM2 operands
+      // k, v, q_j were unscaled, and the output is bf16.
+      bool ok_e = true;
+      const int nparts = final_ ? 2 : 1;
+#pragma unroll 1
+      for (int part = 0; part < nparts; ++part) {
+        if (part == 1) {
           tc_fence_before();
           mbar_arrive(bar(kBarOFree, g));
-          if (!wait_bar_warp(bar(kBarOFull, g), eparts[g] & 1, guard)) break;
+          if (!wait_bar_warp(bar(kBarOFull, g), eparts[g] & 1, guard)) {
+            ok_e = false;
+            break;
+          }
           tc_fence_after();
           ++eparts[g];
-          stage_row<BF16, NH>(A, row, tO, scale_out * (FP8 ? __ldg(p.vsc + head) : 1.0f));
         }
-      } else if (kind == KIND_L) {
-        // cr[k][j] = sum_l P[l][k] (the N = 16 GEMM into S[g]; read it first,
-        // then let the next GEMM1 of this group overwrite S[g]) (:32)
-        uint32_t o[32];
-        tmem_ld32(tS, o);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(bar(kBarCrTaken, g));
-        // cr[k][j] of this row: k = row % M, j = the row's index
-        p.cr[(size_t)(slot * MM + row % MM) * BB + item * PL + row / MM] = __uint_as_float(o[0]);
-        // ar[k][j] = sum_l P[l][k] q[l*b+j] (:34)
-        stage_row<BF16, NH>(A, row, tO, FP8 ? __ldg(p.qsc + head) : 1.0f);
-      } else {
-        // z[l*b + j] = (P y_j) / sum (ma_torch.py:60-62); e4m3 calls return bf16
-        stage_row<(BF16 || FP8), NH>(A, row, tO, scale_out);
+        if (kind == KIND_L) {
+          // cr[k][j] = sum_l P[l][k] (the N = 16 GEMM into S[g]; read it first,
+          // then let the next GEMM1 of this group overwrite S[g]) (:32)
+          uint32_t o[32];
+          tmem_ld32(tS, o);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(bar(kBarCrTaken, g));
+          // cr[k][j] of this row: k = row % M, j = the row's index
+          p.cr[(size_t)(slot * MM + row % MM) * BB + item * PL + row / MM] = __uint_as_float(o[0]);
+        }
+        float sc;
+        if (kind == KIND_R)
+          sc = part == 0 ? p.sm_scale * scale_out * (FP8 ? __ldg(p.ksc + head) : 1.0f)
+                         : scale_out * (FP8 ? __ldg(p.vsc + head) : 1.0f);
+        else
+          sc = kind == KIND_L ? (FP8 ? __ldg(p.qsc + head) : 1.0f) : scale_out;
+        const uint32_t dst = (final_ && part == 0) ? B : A;
+        if (FP8 && kind == KIND_O)
+          stage_row<true, NH>(dst, row, tO, sc);
+        else
+          stage_row<BF16, NH>(dst, row, tO, sc);
+      }
+      if (!ok_e) break;
+      if (kind == KIND_O) {
         // y_j has no other reader: drop it from L2 (GEMM2 consumed it)
         const char* ytile = p.y + ((size_t)slot * BB * MM + item * kT) * DD * 2;
 #pragma unroll
