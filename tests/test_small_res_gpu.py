@@ -3,10 +3,10 @@ intermediates in shared memory, q / k / v staged per item) against the fp32
 oracle, over every (R-item rows, L-item rows) tile pair of 16 / 32, head dims
 64 and 128, masks, front / back padding, T = 1 / 2 / 3, bf16 and fp16, and
 b * M both even and odd (the shared-memory layout's alignment).  Each case
-also runs the workspace small-block kernel
-(MA_DISABLE_SMALL_RES=1) on the same inputs, whose result must agree within
-the same tolerance.  Tolerances as in test_parity_gpu.py (bf16 / fp16 within
-2e-2 * max|ref| of the fp32 reference on the same rounded inputs)."""
+also runs the workspace small-block kernel (MA_DISABLE_SMALL_RES=1) on the
+same inputs, whose result must agree within the same tolerance.
+Tolerances as in test_parity_gpu.py (bf16 / fp16 within 2e-2 * max|ref| of
+the fp32 reference on the same rounded inputs)."""
 import numpy as np
 import pytest
 import torch
