@@ -182,9 +182,10 @@ enum Kind : int { KIND_R = 0, KIND_L = 1, KIND_O = 2 };
 
 // Optional per-tile timeline (compiled in with -DMA_TC_TRACE): for the first
 // kTraceItems tiles of each CTA, slot 0 holds (head, phase, tile) and the
-// other slots globaltimer stamps: 1 claim, 2 dependency met, 3 GEMM1 issued,
-// 4 softmax start, 5 P ready, 6 epilogue start, 15 output staged,
-// 7 published.
+// other slots globaltimer stamps: 1 claim, 2 dependency met (loads issued),
+// 11 loads landed, 3 GEMM1 issued, 4 softmax start, 5 P ready, 8 GEMM2
+// issued, 6 epilogue start, 15 output staged, 12 store issued, 9 store read,
+// 10 writes complete, 7 published.
 #ifdef MA_TC_TRACE
 constexpr int kTraceItems = 256;
 constexpr int kTraceSlots = 16;
@@ -557,6 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         const int e = m % kEntries, gm = m & 1;
         ok = wait_bar(bar(kBarFull, e), (m / kEntries) & 1, guard);
         if (!ok) break;
+        trace_stamp(p, m, 11, globaltimer());
         if (m >= *n_end_s) break;  // end marker: no tile m
         if (FP8) ok = wait_bar(bar(kBarConv, e), (m / kEntries) & 1, guard);  // e4m3 -> f16 done
         if (ok && m >= 2) ok = wait_bar(bar(kBarG2, gm), ((m - 2) >> 1) & 1, guard);
@@ -956,6 +958,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
         if (row == 0 && ok2) ok2 = issue_part(1);
       }
       if (row == 0 && ok2) {
+        trace_stamp(p, n, 8, globaltimer());
         tc_fence_before();
         mbar_arrive(bar(kBarG2, g));
       }
@@ -1118,9 +1121,12 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
           }
         }
         bulk_commit();
+        trace_stamp(p, n, 12, globaltimer());
         bulk_wait_read<0>();  // staging read: the ring entry can be refilled
+        trace_stamp(p, n, 9, globaltimer());
         mbar_arrive(bar(kBarEmpty, e));
         bulk_wait<0>();       // writes complete
+        trace_stamp(p, n, 10, globaltimer());
         fence_proxy_async_global();
         red_release_add(ctrl + kCtrlDone + head * P + ph, 1u);
         trace_stamp(p, n, 7, globaltimer());
