@@ -168,12 +168,16 @@ bool tc_fp8_direct(const ma_fwd_params* p, const Shape& s) {
 // flight give a longer distance between dependent tiles (a round is
 // 2T * hgroup * tiles tiles).  Measured best on B200 for b = M = 128
 // (1: 856 us, 2: 785 us, 3: 808 us, 4: 803 us): rounds of 256 tiles per
-// phase, the same round length for the other shapes.  MA_TC_GROUP
-// overrides it.
+// phase, the same round length for the other shapes.  A call with no more
+// heads than that group's slots (a shard of a few heads per GPU) runs them
+// as two groups instead: the wavefront then has P + 1 rounds, and every
+// round is a dependent step on the critical path (8 heads of b = M = 128:
+// groups of 1: 132 us, 2: 116 us, 4: 107 us).  MA_TC_GROUP overrides it.
 int tc_hgroup(const Shape& s) {
   const int nheads = s.E * s.H;
   const int tiles = s.b * s.M / tc::kT;
   int hgroup = 256 / tiles > 1 ? 256 / tiles : 1;
+  if (nheads <= hgroup * (2 * s.T + 1) && (nheads + 1) / 2 > hgroup) hgroup = (nheads + 1) / 2;
   const char* hg = getenv("MA_TC_GROUP");
   if (hg) hgroup = atoi(hg);
   if (hgroup < 1) hgroup = 1;
@@ -220,9 +224,10 @@ cudaError_t run_tc(const ma_fwd_params* p, const Shape& s, const WsLayout& ws, c
   const int tiles = s.b * s.M / kT;  // tiles per (head, phase)
   int hgroup = tc_hgroup(s);
   // The workspace holds the arrays of ws.tc_slots heads (tc_slots() for
-  // ma_fwd's layout): shrink the group to what exists.
+  // ma_fwd's layout): shrink the group to what exists.  When every head has
+  // a slot of its own, no slot is reused and any group size is safe.
   const int max_slots = ws.tc_slots > 0 && ws.tc_slots < nheads ? ws.tc_slots : nheads;
-  if (hgroup * (2 * s.T + 1) > max_slots)
+  if (max_slots < nheads && hgroup * (2 * s.T + 1) > max_slots)
     hgroup = max_slots / (2 * s.T + 1) > 1 ? max_slots / (2 * s.T + 1) : 1;
   int slots = hgroup * (2 * s.T + 1);
   if (slots > max_slots) slots = max_slots;

@@ -130,7 +130,7 @@ def tc_params(E=4, H=16, N=16384, b=128, T=2, D=128):
 
 
 @pytest.mark.parametrize("E,H,N,b,T", [(4, 16, 16384, 128, 2), (4, 16, 4096, 64, 2),
-                                       (1, 3, 16384, 128, 3)])
+                                       (1, 3, 16384, 128, 3), (1, 8, 16384, 128, 2)])
 def test_tc_workspace_holds_only_the_cycled_slots(E, H, N, b, T):
     """The persistent tcgen05 kernel cycles through at most 2 x (2T+1) head
     slots of al / y / ar / cl / cr (hgroup heads per wavefront phase: 2 at

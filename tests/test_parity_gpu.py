@@ -383,6 +383,17 @@ def test_full_size_properties(name, cuda_device):
     torch.cuda.synchronize()
     check_status(cuda_device)
     assert torch.equal(o4, shuf(o1))
+    # a shard of a few heads (the multi-GPU split: 8 or 16 heads per GPU)
+    # runs with another wavefront group size and slot count: same bits
+    if mask is None:
+        for lo, hi in ((0, 8), (16, 32)):
+            def sl(t):
+                return t.reshape(E * H, 1, *t.shape[2:])[lo:hi]
+
+            o5 = f(sl(q), sl(k), sl(v))
+            torch.cuda.synchronize()
+            check_status(cuda_device)
+            assert torch.equal(o5, sl(o1)), (lo, hi)
 
 
 def test_module_forward_matches_function(cuda_device):
