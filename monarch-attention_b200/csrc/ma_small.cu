@@ -141,21 +141,34 @@ struct WarpTiles {
   static constexpr int kBitmapBytes = kMaxTokens / 8 < 16 ? 16 : kMaxTokens / 8;
 };
 
-// Copy rows [0, ROWS) of an operand into a tile; row r comes from `src(r)`
-// (nullptr = zero row).  Only the first D columns are written; the padding
-// columns D..DP stay zero from the kernel prologue.
-template <int DP, int ROWS, typename F>
-__device__ __forceinline__ void stage_rows(uint32_t tile, int D, int lane, F src) {
+// Copy rows r = 0 .. ROWS-1 of an operand into a tile.  Row r starts at src +
+// r * rstride bytes and is copied when r < rows and its token index n0 + r *
+// nstep lies in [0, N) (workspace rows: n0 = nstep = 0, N = 1); other rows
+// are zero-filled.  Only the first D columns are written; the padding
+// columns D..DP stay zero from the kernel prologue.  Lane (rl, c) copies
+// 16-byte chunk c of rows rl, rl + RPI, ...: every row address is affine in
+// r, so a pass costs three additions and no per-chunk index arithmetic.
+template <int DP, int ROWS>
+__device__ __forceinline__ void stage_rows(uint32_t tile, int D, int lane, const char* src,
+                                           int64_t rstride, int rows, int n0, int nstep, int N,
+                                           const void* safe) {
   constexpr int RS = DP + 8;
-  constexpr int CH = DP / 8;  // 16-byte chunks per padded row
-  const int chunks = D / 8;
+  constexpr int CH = DP / 8;    // 16-byte chunks per padded row
+  constexpr int RPI = 32 / CH;  // rows per pass of the warp
+  const int rl = lane / CH, c = lane - rl * CH;
+  if (rl >= RPI || c >= D / 8) return;
+  const char* s = src + rl * rstride + c * 16;
+  uint32_t d = tile + (uint32_t)(rl * RS + c * 8) * 2;
+  int n = n0 + rl * nstep;
 #pragma unroll
-  for (int idx = lane; idx < ROWS * CH; idx += 32) {
-    const int r = idx / CH, c = idx - r * CH;
-    if (c < chunks) {
-      const char* s = src(r);
-      cp_async16(tile + (r * RS + c * 8) * 2, s ? s + c * 16 : s, s != nullptr);
+  for (int r0 = 0; r0 < ROWS; r0 += RPI) {
+    if (r0 + RPI <= ROWS || r0 + rl < ROWS) {
+      const bool ok = r0 + rl < rows && (unsigned)n < (unsigned)N;
+      cp_async16(d, ok ? s : safe, ok);
     }
+    s += RPI * rstride;
+    d += RPI * RS * 2;
+    n += RPI * nstep;
   }
 }
 
@@ -179,36 +192,34 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
   const int C = R;            // columns
   const size_t esz = sizeof(TI);
 
-  auto tok = [&](const void* base, const int64_t* st, int pidx) -> const char* {
-    const int n = pidx - p.pad_off;
-    if (n < 0 || n >= p.N) return nullptr;
-    return reinterpret_cast<const char*>(base) +
-           esz * ((int64_t)e * st[0] + (int64_t)h * st[1] + (int64_t)n * st[2]);
-  };
   const char* al_h = p.al + (size_t)eh * b * M * D * esz;
   const char* y_h = p.y + (size_t)eh * b * M * D * esz;
   const char* ar_h = p.ar + (size_t)eh * M * b * D * esz;
-  const float* cl_h = p.cl + (size_t)eh * b * M;
   const float* cr_h = p.cr + (size_t)eh * M * b;
+  const float* cl_h = p.cl + (size_t)eh * b * M;
+  // q / k / v rows: token n0 + r * nstep of the head (padded index minus the
+  // pre-padding), zero rows outside the sequence
+  auto stage_tok = [&](uint32_t tile, const void* base, const int64_t* st, int n0, int nstep) {
+    const char* hb = reinterpret_cast<const char*>(base) + esz * (e * st[0] + h * st[1]);
+    stage_rows<DP, ROWS>(tile, D, lane, hb + (int64_t)n0 * st[2] * (int64_t)esz,
+                         st[2] * (int64_t)esz * nstep, R, n0, nstep, p.N, hb);
+  };
+  // workspace rows: row r at base + r * D elements, all R rows valid
+  auto stage_ws = [&](uint32_t tile, const char* base) {
+    stage_rows<DP, ROWS>(tile, D, lane, base, (int64_t)D * esz, R, 0, 0, 1, base);
+  };
 
   // ---- stage operands ----
   if (rph) {
     if (first)
-      stage_rows<DP, ROWS>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, item * b + r) : nullptr; });
+      stage_tok(tA, p.q, p.qs, item * b - p.pad_off, 1);  // q block m
     else
-      stage_rows<DP, ROWS>(tA, D, lane, [&](int r) {
-        return r < R ? ar_h + ((size_t)item * b + r) * D * esz : nullptr;
-      });
-    stage_rows<DP, ROWS>(tB, D, lane, [&](int r) { return r < C ? tok(p.k, p.ks, item * b + r) : nullptr; });
+      stage_ws(tA, ar_h + (size_t)item * b * D * esz);   // ar[m][.]
+    stage_tok(tB, p.k, p.ks, item * b - p.pad_off, 1);    // k block m
   } else {
-    stage_rows<DP, ROWS>(tA, D, lane, [&](int r) { return r < R ? tok(p.q, p.qs, r * b + item) : nullptr; });
-    stage_rows<DP, ROWS>(tB, D, lane, [&](int r) {
-      return r < C ? al_h + ((size_t)item * M + r) * D * esz : nullptr;
-    });
-    if (PH == PH_O)
-      stage_rows<DP, ROWS>(tX, D, lane, [&](int r) {
-        return r < C ? y_h + ((size_t)item * M + r) * D * esz : nullptr;
-      });
+    stage_tok(tA, p.q, p.qs, item - p.pad_off, b);        // Q_j: tokens l * b + j
+    stage_ws(tB, al_h + (size_t)item * M * D * esz);     // al[j][.]
+    if (PH == PH_O) stage_ws(tX, y_h + (size_t)item * M * D * esz);  // y[j][.]
   }
   if (!(rph && first)) {  // the item's cr / cl vector (one fp32 per lane, 0 beyond it)
     const float* vsrc = rph ? cr_h + (size_t)item * b : cl_h + (size_t)item * M;
@@ -245,7 +256,7 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
   for (int nt = 0; nt < NT; ++nt) colsum[nt][0] = colsum[nt][1] = 0.0f;
   const int nparts = PH == PH_RF ? 2 : 1;
   if (PH == PH_RF) {  // V[m] for the second output part, staged with the item
-    stage_rows<DP, ROWS>(tX, D, lane, [&](int r) { return r < C ? tok(p.v, p.vs, item * b + r) : nullptr; });
+    stage_tok(tX, p.v, p.vs, item * b - p.pad_off, 1);
     cp_async_wait_all();
     __syncwarp();
   }

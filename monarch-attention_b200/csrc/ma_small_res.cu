@@ -102,19 +102,29 @@ __device__ __forceinline__ bool vbit(const uint32_t* bits, int pidx) {
 
 // Stage rows t = 0 .. R-1 of a q / k / v operand into a tile (view f = 0):
 // row t is padded token tok0 + t * tstep when t < rows, zero otherwise.
+// Lane (rl, c) copies 16-byte chunk c of rows rl, rl + RPI, ...; the source
+// address is affine in t, and as RPI (2 or 4) divides 8 and rl < RPI, the
+// swizzled position (c ^ t) & 7 of row t0 + rl is ((c ^ rl) & 7) ^ (t0 & 7),
+// a constant per pass.
 template <int DP, int R>
 __device__ __forceinline__ void stage(const View& dst, const char* base, int64_t stride_b,
                                       const Params& p, int tok0, int tstep, int rows, int lane) {
   constexpr int CH = DP / 8;
   constexpr int RPI = 32 / CH;  // rows per pass of the warp
-  const int c = lane % CH;
+  static_assert(RPI == 2 || RPI == 4, "staging passes of 2 or 4 rows");
+  const int rl = lane / CH, c = lane % CH;
+  int n = tok0 + rl * tstep - p.pad_off;
+  const char* s = base + n * stride_b + c * 16;
+  const int64_t step = RPI * tstep * stride_b;
+  const uint32_t d0 = dst.base + (uint32_t)rl * dst.stride + ((uint32_t)(c >> 3) << 7);
+  const uint32_t x = (uint32_t)((c ^ rl) & 7);
 #pragma unroll
   for (int t0 = 0; t0 < R; t0 += RPI) {
-    const int t = t0 + lane / CH;
-    const int n = tok0 + t * tstep - p.pad_off;
-    const bool ok = t < rows && n >= 0 && n < p.N;
-    const char* src = ok ? base + n * stride_b + c * 16 : base;
-    cp_async16(dst.chunk(t, c), src, ok);
+    const bool ok = t0 + rl < rows && (unsigned)n < (unsigned)p.N;
+    cp_async16(d0 + (uint32_t)t0 * dst.stride + ((x ^ (uint32_t)(t0 & 7)) << 4), ok ? s : base,
+               ok);
+    s += step;
+    n += RPI * tstep;
   }
 }
 
