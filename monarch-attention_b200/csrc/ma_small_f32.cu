@@ -91,19 +91,33 @@ struct Tiles {
   static constexpr int kBitmapBytes = kMaxTokens / 8 < 16 ? 16 : kMaxTokens / 8;
 };
 
-// rows [0, ROWS) of an operand into a tile: row r from src(r) (nullptr =
-// zero row), the first D floats of each row in 16-byte pieces
-template <int DP, int ROWS, typename F>
-__device__ __forceinline__ void stage_rows(uint32_t tile, int D, int lane, F src) {
+// Rows r = 0 .. ROWS-1 of an operand into a tile, the first D floats of each
+// row in 16-byte pieces.  Row r starts at src + r * rstride floats and is
+// copied when r < rows and its token index n0 + r * nstep lies in [0, N)
+// (workspace rows: n0 = nstep = 0, N = 1); other rows are zero-filled.  Lane
+// (rl, c) copies piece c of rows rl, rl + RPI, ...: the row address is
+// affine in r, so a pass costs three additions.
+template <int DP, int ROWS>
+__device__ __forceinline__ void stage_rows(uint32_t tile, int D, int lane, const float* src,
+                                           int64_t rstride, int rows, int n0, int nstep, int N,
+                                           const float* safe) {
   constexpr int RS = DP + 4;
-  constexpr int CH = DP / 4;
-  const int chunks = D / 4;
-  for (int idx = lane; idx < ROWS * CH; idx += 32) {
-    const int r = idx / CH, c = idx - r * CH;
-    if (c < chunks) {
-      const float* s = src(r);
-      cp_async16(tile + (r * RS + c * 4) * 4, s ? s + c * 4 : s, s != nullptr);
+  constexpr int CH = DP / 4;    // 16-byte pieces per padded row
+  constexpr int RPI = 32 / CH;  // rows per pass of the warp
+  const int rl = lane / CH, c = lane - rl * CH;
+  if (rl >= RPI || c >= D / 4) return;
+  const float* s = src + rl * rstride + c * 4;
+  uint32_t d = tile + (uint32_t)(rl * RS + c * 4) * 4;
+  int n = n0 + rl * nstep;
+#pragma unroll 8
+  for (int r0 = 0; r0 < ROWS; r0 += RPI) {
+    if (r0 + RPI <= ROWS || r0 + rl < ROWS) {
+      const bool ok = r0 + rl < rows && (unsigned)n < (unsigned)N;
+      cp_async16(d, ok ? s : safe, ok);
     }
+    s += RPI * rstride;
+    d += RPI * RS * 4;
+    n += RPI * nstep;
   }
 }
 
@@ -129,41 +143,35 @@ __device__ void run_item(const Params& p, int e, int h, int item, int first, flo
   const int R = rph ? b : M;  // rows of the item
   const int C = R;            // columns
 
-  auto tok = [&](const float* base, const int64_t* st, int pidx) -> const float* {
-    const int n = pidx - p.pad_off;
-    if (n < 0 || n >= p.N) return nullptr;
-    return base + ((int64_t)e * st[0] + (int64_t)h * st[1] + (int64_t)n * st[2]);
-  };
   const float* al_h = p.al + (size_t)eh * b * M * D;
   const float* y_h = p.y + (size_t)eh * b * M * D;
   const float* ar_h = p.ar + (size_t)eh * M * b * D;
   const float* cl_h = p.cl + (size_t)eh * b * M;
   const float* cr_h = p.cr + (size_t)eh * M * b;
+  // q / k / v rows: token n0 + r * nstep of the head (padded index minus the
+  // pre-padding), zero rows outside the sequence
+  auto stage_tok = [&](uint32_t tile, const float* base, const int64_t* st, int n0, int nstep) {
+    const float* hb = base + ((int64_t)e * st[0] + (int64_t)h * st[1]);
+    stage_rows<DP, ROWS>(tile, D, lane, hb + (int64_t)n0 * st[2], st[2] * nstep, R, n0, nstep,
+                         p.N, hb);
+  };
+  // workspace rows: row r at base + r * D floats, all R rows valid
+  auto stage_ws = [&](uint32_t tile, const float* base) {
+    stage_rows<DP, ROWS>(tile, D, lane, base, D, R, 0, 0, 1, base);
+  };
 
   // ---- stage operands (same roles as the 16-bit kernel) ----
   if (rph) {
     if (first)
-      stage_rows<DP, ROWS>(tA, D, lane,
-                           [&](int r) { return r < R ? tok(p.q, p.qs, item * b + r) : nullptr; });
+      stage_tok(tA, p.q, p.qs, item * b - p.pad_off, 1);  // q block m
     else
-      stage_rows<DP, ROWS>(tA, D, lane, [&](int r) {
-        return r < R ? ar_h + ((size_t)item * b + r) * D : nullptr;
-      });
-    stage_rows<DP, ROWS>(tB, D, lane,
-                         [&](int r) { return r < C ? tok(p.k, p.ks, item * b + r) : nullptr; });
-    if (PH == PH_RF)
-      stage_rows<DP, ROWS>(tX, D, lane,
-                           [&](int r) { return r < C ? tok(p.v, p.vs, item * b + r) : nullptr; });
+      stage_ws(tA, ar_h + (size_t)item * b * D);         // ar[m][.]
+    stage_tok(tB, p.k, p.ks, item * b - p.pad_off, 1);    // k block m
+    if (PH == PH_RF) stage_tok(tX, p.v, p.vs, item * b - p.pad_off, 1);  // v block m
   } else {
-    stage_rows<DP, ROWS>(tA, D, lane,
-                         [&](int r) { return r < R ? tok(p.q, p.qs, r * b + item) : nullptr; });
-    stage_rows<DP, ROWS>(tB, D, lane, [&](int r) {
-      return r < C ? al_h + ((size_t)item * M + r) * D : nullptr;
-    });
-    if (PH == PH_O)
-      stage_rows<DP, ROWS>(tX, D, lane, [&](int r) {
-        return r < C ? y_h + ((size_t)item * M + r) * D : nullptr;
-      });
+    stage_tok(tA, p.q, p.qs, item - p.pad_off, b);        // Q_j: tokens l * b + j
+    stage_ws(tB, al_h + (size_t)item * M * D);           // al[j][.]
+    if (PH == PH_O) stage_ws(tX, y_h + (size_t)item * M * D);  // y[j][.]
   }
   if (!(rph && first)) {  // the item's cr / cl vector (0 beyond it)
     const float* vsrc = rph ? cr_h + (size_t)item * b : cl_h + (size_t)item * M;
