@@ -216,10 +216,20 @@ class ClockSampler:
                 stdout=self.f, stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        # wait (at most 5 s) for the first sample: with one sampler per rank
+        # starting at once, nvidia-smi's start-up can outlast a short timed
+        # region, which then had no sample at all
+        t0 = time.time()
+        while time.time() - t0 < 5.0 and self.proc.poll() is None:
+            if os.path.getsize(self.path) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.12)  # let the samples taken at the end of the region land
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
