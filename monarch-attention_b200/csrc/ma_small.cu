@@ -295,7 +295,7 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
       float c = 1.0f;
       if (rph) {
         const float crj = (first || r >= R) ? 1.0f : vec[r];
-        c = p.sm_scale / (crj + kEps);  // t = sm_scale * S / (cr + eps), ma_torch.py:11-12
+        c = __fdividef(p.sm_scale, crj + kEps);  // t = sm_scale * S / (cr + eps), ma_torch.py:11-12
       }
       // pass 1: row maximum (R: of S, as c > 0 gives max t = c * max S)
       float mx = -INFINITY;
@@ -337,13 +337,13 @@ __device__ void run_item(const SmallParams& p, int e, int h, int item, int first
         wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
         wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
         const float den = sum + kEps;  // r = e / (sum + eps), :17
-        const float inv = 1.0f / den;
+        const float inv = __fdividef(1.0f, den);
         // sum_i r_i log r_i, log r_i = ln2 * u_i - log(den) (:20)
         cl_row[hf] = kLn2S * inv * wsum - __logf(den) * sum * inv;
         row_scale[hf] = inv;
       } else {
         cl_row[hf] = 0.0f;
-        row_scale[hf] = 1.0f / sum;
+        row_scale[hf] = __fdividef(1.0f, sum);
       }
       if (PH == PH_L) {
         // the L-step's P is normalised here (its column sums are cr, and its

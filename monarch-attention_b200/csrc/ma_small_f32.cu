@@ -228,7 +228,7 @@ __device__ void run_item(const Params& p, int e, int h, int item, int first, flo
     float c = 1.0f;
     if (rph) {
       const float crj = (first || r >= R) ? 1.0f : vec[r];
-      c = p.sm_scale / (crj + kEps);  // t = sm_scale * S / (cr + eps), :11-12
+      c = __fdividef(p.sm_scale, crj + kEps);  // t = sm_scale * S / (cr + eps), :11-12
     }
     float mx = -INFINITY;
 #pragma unroll
@@ -262,19 +262,19 @@ __device__ void run_item(const Params& p, int e, int h, int item, int first, flo
       wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
       wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
       const float den = sum + kEps;  // r = e / (sum + eps), :17
-      const float inv = 1.0f / den;
+      const float inv = __fdividef(1.0f, den);
       // cl[j][m] = sum_i r_i log r_i, log r_i = ln2 * u_i - log(den) (:20)
       const float clv = kLn2S * inv * wsum - __logf(den) * sum * inv;
       if (cx == 0 && r < R) p.cl[(size_t)eh * b * M + (size_t)r * M + item] = clv;
       row_scale[i] = inv;
     } else if (PH == PH_L) {
       // L: P is normalised here, times the query mask of row l (:28-30)
-      const float sc = (r < R && valid_bit(vbits, r * b + item)) ? 1.0f / sum : 0.0f;
+      const float sc = (r < R && valid_bit(vbits, r * b + item)) ? __fdividef(1.0f, sum) : 0.0f;
 #pragma unroll
       for (int j = 0; j < CT; ++j) s[i][j] *= sc;
       row_scale[i] = 1.0f;
     } else {
-      row_scale[i] = 1.0f / sum;
+      row_scale[i] = __fdividef(1.0f, sum);
     }
   }
   // P -> staging block Pst[r][c] (R / out: unnormalised e, L: normalised)

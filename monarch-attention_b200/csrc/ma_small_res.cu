@@ -254,7 +254,7 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, bo
       float c = 1.0f;
       if (kR) {
         const float crj = (first || r >= R) ? 1.0f : cr[item * b + r];
-        c = p.sm_scale / (crj + kEps);  // t = sm_scale * S / (cr + eps), ma_torch.py:11-12
+        c = __fdividef(p.sm_scale, crj + kEps);  // t = sm_scale * S / (cr + eps), ma_torch.py:11-12
       }
       float mx = -INFINITY;
 #pragma unroll
@@ -295,18 +295,22 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, bo
         wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
         wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
         const float den = sum + kEps;  // r = e / (sum + eps), :17
-        const float inv = 1.0f / den;
+        const float inv = __fdividef(1.0f, den);
         // sum_i r_i log r_i, log r_i = ln2 * u_i - log(den) (:20)
         cl_row[hf] = kLn2 * inv * wsum - __logf(den) * sum * inv;
         row_scale[hf] = inv;
       } else {
         cl_row[hf] = 0.0f;
-        row_scale[hf] = 1.0f / sum;
+        row_scale[hf] = __fdividef(1.0f, sum);
       }
-      if (PH == PH_L) {
-        // normalised P, times the query mask of row l (:30)
+      {
+        // P is normalised before it is packed for the second matmul (the
+        // reference's r.to(dtype) / l.to(dtype)): L rows times the query
+        // mask of row l (:30); a plain R-step's rows also carry al's
+        // sm_scale (:21), so no output scales
         float sc = row_scale[hf];
-        if (!(r < R && vbit(vbits, r * b + item))) sc = 0.0f;
+        if (PH == PH_L && !(r < R && vbit(vbits, r * b + item))) sc = 0.0f;
+        if (PH == PH_R) sc *= p.sm_scale;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -371,21 +375,21 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, bo
         for (int hf = 0; hf < 2; ++hf) {
           const int r = mt * 16 + g + 8 * hf;
           if (r >= R) continue;
-          float sc = row_scale[hf];  // 1 / (sum + eps) of R rows, 1 / sum of out rows
+          // P is normalised already (and carries sm_scale in a plain
+          // R-step): only the final R-step's al part is scaled here
+          const bool scaled = PH == PH_RF && part == 0;
+          const float sc = p.sm_scale;
           if (kR) {
             // al[j][m] = sm_scale * (r K[m]) (:21) -> al row (j, m);
             // y[j][m] = r V[m] (:51) -> ary row (m, j)
-            View dst;
-            if (part == 0) {
-              dst = View{s_al + (uint32_t)(item * RBY), (uint32_t)(M * RBY), item};
-              sc *= p.sm_scale;
-            } else {
-              dst = View{s_ary + (uint32_t)(item * b * RBY), RBY, item};
-            }
+            const View dst = part == 0
+                ? View{s_al + (uint32_t)(item * RBY), (uint32_t)(M * RBY), item}
+                : View{s_ary + (uint32_t)(item * b * RBY), RBY, item};
 #pragma unroll
             for (int nd = 0; nd < ND; ++nd)
               st_shared_b32(dst.chunk(r, nd) + 4 * t4,
-                            pack2<BF16>(o[nd][2 * hf] * sc, o[nd][2 * hf + 1] * sc));
+                            scaled ? pack2<BF16>(o[nd][2 * hf] * sc, o[nd][2 * hf + 1] * sc)
+                                   : pack2<BF16>(o[nd][2 * hf], o[nd][2 * hf + 1]));
           } else {
             // z at token l * b + j (:60-62, :106-108)
             const int n = r * b + item - p.pad_off;
@@ -395,7 +399,7 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, bo
 #pragma unroll
             for (int nd = 0; nd < ND; ++nd)
               *reinterpret_cast<uint32_t*>(dst + (nd * 8 + 2 * t4) * esz) =
-                  pack2<BF16>(o[nd][2 * hf] * sc, o[nd][2 * hf + 1] * sc);
+                  pack2<BF16>(o[nd][2 * hf], o[nd][2 * hf + 1]);
           }
         }
       }
