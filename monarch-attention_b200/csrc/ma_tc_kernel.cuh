@@ -76,12 +76,12 @@ constexpr int kStoreWarp = 14;     // warps 14, 15: TMA stores + publication (al
 constexpr int kStoreWarps = 2;
 constexpr int kT = 128;                  // tile rows (and logit columns)
 constexpr int kHalf = 16384;             // one 64-column half of a tile (128 rows x 128 B)
-constexpr int kEntries = 3;              // ring entries (tiles in flight)
+constexpr int kMaxEntries = 4;           // ring entries (tiles in flight): 3 at D = 128, 4 at D = 64
 constexpr int kItemRing = 8;             // tile descriptors for the epilogue
 constexpr int kScaleRing = 4;            // per-row output scales, softmax -> epilogue
 // small objects at the start of dynamic shared memory
 constexpr int kOffBar = 0;        // mbarriers
-constexpr int kOffDesc = 256;     // tile descriptors of the ring entries (kEntries x int4)
+constexpr int kOffDesc = 256;     // tile descriptors of the ring entries (kMaxEntries x int4)
 constexpr int kOffEnd = 320;      // number of tiles this CTA was given (set at the end)
 constexpr int kOffTmem = 324;     // TMEM base address
 constexpr int kOffItems = 384;    // tile descriptors by tile index (kItemRing x int4)
@@ -97,37 +97,42 @@ constexpr int kOffExtA = 3072;    // A_ext (2 KB)
 constexpr int kOffVec = 5120;     // per entry: B_ext rows of cl[j][:] (L / out, 2 KB)
                                   // or the cr[m][:] vector (R, 512 B fp32)
 constexpr int kExtBytes = 2048;
-constexpr int kOffZero = kOffVec + kEntries * kExtBytes;  // 2 KB of zeros
+constexpr int kOffZero = kOffVec + kMaxEntries * kExtBytes;  // 2 KB of zeros
 constexpr int kSmallBytes = kOffZero + kExtBytes;
 
 // bytes of one tile (128 rows of DD 16-bit values), of a ring entry (tile A,
 // then tile B, which also holds the 128 x 128 16-bit P^T of an L tile: at
-// least 32 KB) and of the dynamic shared memory of a CTA
+// least 32 KB) and of the dynamic shared memory of a CTA.  The ring has as
+// many entries as fit: 3 of 64 KB at D = 128, 4 of 48 KB at D = 64 (a tile
+// holds its entry from its loads to the read of its staged output, so the
+// entries in flight bound the tiles per second of an SM).
 __host__ __device__ constexpr int tile_bytes(int dd) { return (dd / 64) * kHalf; }
 __host__ __device__ constexpr int entry_bytes(int dd) { return tile_bytes(dd) + 2 * kHalf; }
+__host__ __device__ constexpr int ring_entries(int dd) { return dd == 64 ? 4 : 3; }
 __host__ __device__ constexpr int smem_bytes(int dd) {
-  return kSmallBytes + 1024 + kEntries * entry_bytes(dd);  // + worst-case alignment pad
+  return kSmallBytes + 1024 + ring_entries(dd) * entry_bytes(dd);  // + worst-case alignment pad
 }
-static_assert(smem_bytes(128) <= 232448, "shared memory budget");
+static_assert(smem_bytes(128) <= 232448 && smem_bytes(64) <= 232448, "shared memory budget");
+static_assert(ring_entries(128) <= kMaxEntries && ring_entries(64) <= kMaxEntries, "ring layout");
 
 // barrier offsets (8 B each)
-constexpr int kBarFull = 0;      // [kEntries] A/B tiles (+ vector) of the entry landed
-constexpr int kBarEmpty = 24;    // [kEntries] the entry's last GEMM finished
-constexpr int kBarX = 48;        // [kEntries] late X tile (V or y) landed
-constexpr int kBarSFull = 72;    // [2] S of the group written (GEMM1 done)
-constexpr int kBarPReady = 88;   // [2] P of the group written (128 arrivals)
-constexpr int kBarOFull = 104;   // [2] O of the group written (one per GEMM2 part)
-constexpr int kBarOFree = 120;   // [2] O of the group read (128 arrivals per part)
-constexpr int kBarCrTaken = 136; // [2] cr read out of S (L tiles, 128 arrivals)
-constexpr int kBarDrain = 160;   // MMA drain before the end
-constexpr int kBarStaged = 168;  // [kEntries] output tile(s) of the entry's tile staged (128)
-constexpr int kBarG2 = 192;      // [2] GEMM2 (all parts) of the group's tile issued
-constexpr int kBarDrain2 = 208;  // [2] MMAs a softmax group issued, complete (at the end)
+constexpr int kBarFull = 0;      // [kMaxEntries] A/B tiles (+ vector) of the entry landed
+constexpr int kBarEmpty = 32;    // [kMaxEntries] the entry's last GEMM finished
+constexpr int kBarX = 64;        // [kMaxEntries] late X tile (V or y) landed
+constexpr int kBarSFull = 96;    // [2] S of the group written (GEMM1 done)
+constexpr int kBarPReady = 112;  // [2] P of the group written (128 arrivals)
+constexpr int kBarOFull = 128;   // [2] O of the group written (one per GEMM2 part)
+constexpr int kBarOFree = 144;   // [2] O of the group read (128 arrivals per part)
+constexpr int kBarCrTaken = 160; // [2] cr read out of S (L tiles, 128 arrivals)
+constexpr int kBarDrain = 176;   // MMA drain before the end
+constexpr int kBarStaged = 184;  // [kMaxEntries] output tile(s) of the entry's tile staged (128)
+constexpr int kBarG2 = 216;      // [2] GEMM2 (all parts) of the group's tile issued
+constexpr int kBarDrain2 = 232;  // [2] MMAs a softmax group issued, complete (at the end)
 // e4m3 inputs (FP8 builds): the item's e4m3 tiles were converted in place to
 // f16 by its softmax group (128 arrivals; GEMM1 waits for it), and the late
 // V tile of a final R-step likewise (per group, before GEMM2's second part)
-constexpr int kBarConv = 224;    // [kEntries]
-constexpr int kBarVConv = 336;   // [2] (after the small objects at 320..327)
+constexpr int kBarConv = 328;    // [kMaxEntries] (after the small objects at 320..327)
+constexpr int kBarVConv = 360;   // [2]
 
 // TMEM columns (fp32, 128 lanes): per group g, S/P at 256 g and O at 256 g + 128
 constexpr uint32_t kTmemCols = 512;
@@ -311,6 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
   constexpr int NH = DD / 64;             // 64-column halves of a D-wide row
   constexpr int kTileBytes = tile_bytes(DD);
   constexpr int kEntryBytes = entry_bytes(DD);  // tiles A and B
+  constexpr int kEntries = ring_entries(DD);     // ring entries of this head dim
   static_assert((BB == 32 || BB == 64 || BB == 128) && (MM == 32 || MM == 64 || MM == 128),
                 "block size and block count 32, 64 or 128");
   static_assert(DD == 64 || DD == 128, "head dim 64 or 128");
@@ -394,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) ma_tc_kernel(const __grid_constan
       int r = 0, ph = 0, sub = 0;
       uint32_t blk = 0;
       uint32_t issued = 0;  // bit e: a load was issued on entry e
-      uint32_t last_on[kEntries] = {0, 0, 0};
+      uint32_t last_on[kEntries] = {};
       // Tiles are claimed p.claim at a time (one global atomic per batch), and
       // the last (head, phase) whose dependency was seen complete is
       // remembered (completion is final), so consecutive tiles of one
