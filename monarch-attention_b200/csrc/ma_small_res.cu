@@ -157,7 +157,8 @@ __device__ __forceinline__ void stage_item(const Params& p, int e, int h, int it
 // columns k).  Rows and columns beyond b (R) or M (L / O) are padding.
 template <int PH, bool BF16, int DP, int RB, int RM>
 __device__ void run_item(const Params& p, int e, int h, int item, bool first, bool staged,
-                         uint8_t* sm, uint32_t t0s, uint32_t t1s, int lane) {
+                         uint8_t* sm, uint32_t t0s, uint32_t t1s, int lane, int mt_lo = 0,
+                         int mt_hi = 2) {
   constexpr bool kR = PH == PH_R || PH == PH_RF;
   constexpr int ROWS = kR ? RB : RM;
   constexpr int MT = ROWS / 16;  // m16 tiles
@@ -225,8 +226,11 @@ __device__ void run_item(const Params& p, int e, int h, int item, bool first, bo
   bool v_staged = PH == PH_RF && !first;
   const int rlast = R - 1;
 
+  // 16-row tiles mt_lo .. mt_hi - 1 of the item (all of them, or one half
+  // of an R item shared by a warp pair)
+  if (mt_hi > MT) mt_hi = MT;
 #pragma unroll 1
-  for (int mt = 0; mt < MT; ++mt) {
+  for (int mt = mt_lo; mt < mt_hi; ++mt) {
     // ---- S row tile = A[mt] B^T ----
     float acc[NT][4];
 #pragma unroll
@@ -465,11 +469,26 @@ __device__ __forceinline__ bool token_valid(const Params& p, int e, int pidx) {
   return mask_value(p.mask, p.mask_dtype, (int64_t)e * p.ms[0] + (int64_t)n * p.ms[1]);
 }
 
-template <bool BF16, int DP, int RB, int RM>
-__global__ void __launch_bounds__(kThreads, (RB == 16 && RM == 16) ? 2 : 1)
+// SPLIT (D = 64, 32-row R items, 16-row L / output items: the RoBERTa
+// shape, whose resident arrays leave room for one CTA per SM): 16 warps in
+// 8 pairs.  A pair shares one staging slot (T0, T1 of 32 rows); its two
+// warps take the two 16-row halves of each R item (row-local softmax, each
+// writing its own rows of al, cl, y), with a named barrier per pair after
+// the shared operands landed and before they are replaced.  L / output
+// items stay one per warp, in the warp's half of the slot (Q_j, then P^T).
+// Twice the warps of the 8-warp layout in the same shared memory.
+__device__ __forceinline__ void pair_sync(int pair) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
+}
+
+template <bool BF16, int DP, int RB, int RM, bool SPLIT>
+__global__ void __launch_bounds__(SPLIT ? 2 * kThreads : kThreads,
+                                  (RB == 16 && RM == 16) ? 2 : 1)
     ma_small_res_kernel(const Params p) {
   extern __shared__ __align__(128) uint8_t sm[];
   constexpr int RT = RB > RM ? RB : RM;
+  constexpr int kW = SPLIT ? 2 * kWarps : kWarps;  // warps of the CTA
+  static_assert(!SPLIT || (DP == 64 && RB == 32 && RM == 16), "pair layout: RoBERTa shape");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int eh = blockIdx.x;
   const int e = eh / p.H, h = eh - e * p.H;
@@ -477,19 +496,65 @@ __global__ void __launch_bounds__(kThreads, (RB == 16 && RM == 16) ? 2 : 1)
   const size_t res = bits_offset(b * M, DP * 2);
   uint32_t* vbits = reinterpret_cast<uint32_t*>(sm + res);
   uint8_t* tiles = sm + res + 128;
-  const uint32_t t0s = smem_u32(tiles + (size_t)warp * 2 * RT * (DP * 2));
+  const int slot = SPLIT ? warp >> 1 : warp;  // staging slot (T0, T1)
+  const uint32_t t0s = smem_u32(tiles + (size_t)slot * 2 * RT * (DP * 2));
   const uint32_t t1s = t0s + RT * (DP * 2);
   trace_stamp(p, eh, 0);
   // token validity of the padded sequence (pad positions and the mask row)
   // (one lane per token, so the mask loads of a word are issued together)
   const int Np = M * b;
-  for (int w = warp; w < (Np + 31) / 32; w += kWarps) {
+  for (int w = warp; w < (Np + 31) / 32; w += kW) {
     const int pidx = w * 32 + lane;
     const uint32_t bits = __ballot_sync(0xffffffffu, pidx < Np && token_valid(p, e, pidx));
     if (lane == 0) vbits[w] = bits;
   }
   __syncthreads();
   trace_stamp(p, eh, 1);
+  if constexpr (SPLIT) {
+    const int pair = warp >> 1, half = warp & 1;
+    constexpr int kPairs = kW / 2;
+    constexpr int RBY = DP * 2;
+    // this warp's half of the slot for L / output items: Q_j, then P^T
+    const uint32_t l0 = t0s + (uint32_t)half * (RT * RBY), l1 = l0 + RM * RBY;
+    const char* qh = reinterpret_cast<const char*>(p.q) + 2 * (e * p.qs[0] + h * p.qs[1]);
+    const char* kh = reinterpret_cast<const char*>(p.k) + 2 * (e * p.ks[0] + h * p.ks[1]);
+    const char* vh = reinterpret_cast<const char*>(p.v) + 2 * (e * p.vs[0] + h * p.vs[1]);
+    for (int t = 0; t < p.T; ++t) {
+      const bool final_ = t == p.T - 1, first = t == 0;
+      for (int m = pair; m < M; m += kPairs) {
+        // half 0 stages T0 (q[m] in the first round, v[m] in the final one),
+        // half 1 stages T1 (k[m])
+        const View T0{t0s, RBY, 0}, T1{t1s, RBY, 0};
+        if (half == 0) {
+          if (first) stage<DP, RB>(T0, qh, 2 * p.qs[2], p, m * b, 1, b, lane);
+          else if (final_) stage<DP, RB>(T0, vh, 2 * p.vs[2], p, m * b, 1, b, lane);
+        } else {
+          stage<DP, RB>(T1, kh, 2 * p.ks[2], p, m * b, 1, b, lane);
+        }
+        cp_async_wait_all();
+        pair_sync(pair);
+        if (final_)
+          run_item<PH_RF, BF16, DP, RB, RM>(p, e, h, m, first, true, sm, t0s, t1s, lane, half,
+                                            half + 1);
+        else
+          run_item<PH_R, BF16, DP, RB, RM>(p, e, h, m, first, true, sm, t0s, t1s, lane, half,
+                                           half + 1);
+        pair_sync(pair);
+      }
+      __syncthreads();
+      trace_stamp(p, eh, 2 + 2 * t);
+      for (int j = warp; j < b; j += kW) {
+        stage_item<PH_L, DP, RB, RM>(p, e, h, j, false, l0, l1, lane);
+        if (final_)
+          run_item<PH_O, BF16, DP, RB, RM>(p, e, h, j, false, true, sm, l0, l1, lane);
+        else
+          run_item<PH_L, BF16, DP, RB, RM>(p, e, h, j, false, true, sm, l0, l1, lane);
+      }
+      __syncthreads();
+      trace_stamp(p, eh, 3 + 2 * t);
+    }
+    return;
+  }
   // Each warp stages the q / k / v rows of its next item as soon as the
   // current one is done -- across phase barriers too (they are inputs) -- so
   // an item waits only for copies issued an item earlier.
@@ -543,15 +608,15 @@ __global__ void __launch_bounds__(kThreads, (RB == 16 && RM == 16) ? 2 : 1)
   }
 }
 
-template <bool BF16, int DP, int RB, int RM>
+template <bool BF16, int DP, int RB, int RM, bool SPLIT = false>
 static cudaError_t launch(const Params& sp, cudaStream_t st) {
   constexpr int RT = RB > RM ? RB : RM;
   const size_t smem = smem_bytes<DP>(sp.b, sp.M, RT);
-  auto kfn = ma_small_res_kernel<BF16, DP, RB, RM>;
+  auto kfn = ma_small_res_kernel<BF16, DP, RB, RM, SPLIT>;
   cudaError_t err =
       cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  kfn<<<sp.E * sp.H, kThreads, smem, st>>>(sp);
+  kfn<<<sp.E * sp.H, SPLIT ? 2 * kThreads : kThreads, smem, st>>>(sp);
   return cudaGetLastError();
 }
 
@@ -615,6 +680,13 @@ cudaError_t run_small_res(const ma_fwd_params* p, const Shape& s, cudaStream_t s
     err = bf ? smallr::launch<true, DPV, RBV, RMV>(sp, st)                                \
              : smallr::launch<false, DPV, RBV, RMV>(sp, st);
   MA_RES_CASE(64, 16, 16)
+  // D = 64, 32-row R items, 16-row L items (RoBERTa): the 16-warp pair
+  // layout (MA_SMALL_RES_PAIRS=0 selects the 8-warp one)
+  const char* pairs = getenv("MA_SMALL_RES_PAIRS");
+  if (s.D == 64 && rb == 32 && rm == 16 && !(pairs && pairs[0] == '0')) {
+    err = bf ? smallr::launch<true, 64, 32, 16, true>(sp, st)
+             : smallr::launch<false, 64, 32, 16, true>(sp, st);
+  } else
   MA_RES_CASE(64, 32, 16)
   MA_RES_CASE(64, 16, 32)
   MA_RES_CASE(64, 32, 32)

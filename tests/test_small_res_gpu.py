@@ -92,3 +92,27 @@ def test_small_res_deterministic(cuda_device):
     b = monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, impl="small")
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("name,base,over", [
+    ("roberta", "roberta_bf16", dict(E=2, H=3)),
+    ("roberta_T3_f16", "roberta_bf16", dict(E=1, H=2, T=3, dtype="f16")),
+    ("b17_M12", "roberta_bf16", dict(E=2, H=2, N=204, B=17, mask_min_len=100)),
+    ("b20_M10_prepad", "roberta_bf16", dict(E=1, H=2, N=195, B=20, pre_pad=True)),
+], ids=lambda x: x if isinstance(x, str) else None)
+def test_small_res_warp_pairs_match_single_warps(name, base, over, cuda_device, monkeypatch):
+    """The 16-warp layout (a warp pair shares the staged k / v / q tiles of
+    an R item and takes one 16-row half each) computes every row exactly as
+    the 8-warp layout does: the same bits."""
+    cfg = CONFIGS[base].with_(**over)
+    q, k, v, mask, _ = make_inputs(cfg, device=cuda_device)
+
+    def run():
+        return monarch_attention(q, k, v, mask, cfg.T, cfg.B, cfg.pre_pad, impl="small")
+
+    pairs = run()
+    monkeypatch.setenv("MA_SMALL_RES_PAIRS", "0")
+    single = run()
+    torch.cuda.synchronize()
+    assert mab.read_status(cuda_device) == 0
+    assert torch.equal(pairs, single)
