@@ -1,8 +1,8 @@
 // Fused small-block MonarchAttention forward: one thread-block cluster runs
 // every phase of one (batch, head) -- the T-1 (R, L) rounds, the final
 // R-step and the output step of ma/ma_torch.py:100-105 -- with a cluster
-// barrier between phases and no kernel boundaries.  The cluster's CTAs (1, 2
-// or 4) take turns on the items of a phase, so a head's critical path is
+// barrier between phases and no kernel boundaries.  The cluster's CTAs (1, 2,
+// 4 or 8) take turns on the items of a phase, so a head's critical path is
 // shorter and the grid packs into fewer partial waves.  For block size b <= 32 and number of blocks M <= 32
 // (the ViT, RoBERTa and DiT shapes), D = Dv <= 128, bf16 / fp16, any strides,
 // padding and key-padding mask.
@@ -542,21 +542,23 @@ __global__ void __launch_bounds__(kThreads, ROWS == 16 ? 4 : 3) ma_small_kernel(
   }
 }
 
-// CTAs per head (1, 2 or 4).  CTAs of equal length run in waves of `slots`
+// CTAs per head (1, 2, 4 or 8).  CTAs of equal length run in waves of `slots`
 // (resident CTAs on the GPU), so a forward takes about
 // ceil(heads * C / slots) waves of 1 / C of a head's work; each doubling of
 // C costs ~10 % in cluster barriers and idle warps (a phase has only 14-32
 // items).  Measured on B200: ViT (768 heads) best at 2, RoBERTa (384 heads,
-// one wave) at 1, DiT (512 heads) at 4.  MA_SMALL_CLUSTER overrides.
-static int cluster_size(int heads, int slots) {
+// one wave) at 1, DiT (512 heads) at 4, BART-1k (48 heads) at 8.
+// MA_SMALL_CLUSTER overrides.
+static int cluster_size(int heads, int slots, int items) {
   const char* env = getenv("MA_SMALL_CLUSTER");
   if (env) {
     const int c = atoi(env);
-    if (c == 1 || c == 2 || c == 4) return c;
+    if (c == 1 || c == 2 || c == 4 || c == 8) return c;
   }
   int best_c = 1;
   double best = 1e300;
-  for (int c = 1, lg = 0; c <= 4; c *= 2, ++lg) {
+  // up to 8 CTAs, while the cluster's warps have an item each in every phase
+  for (int c = 1, lg = 0; c <= 8 && (c == 1 || c * kWarps <= items); c *= 2, ++lg) {
     const int64_t waves = ((int64_t)heads * c + slots - 1) / slots;
     const double cost = (double)waves / c * (1.0 + 0.1 * lg);
     if (cost < best - 1e-9) {
@@ -581,7 +583,7 @@ static cudaError_t launch(const SmallParams& sp, cudaStream_t st) {
   err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (err != cudaSuccess) return err;
   const int heads = sp.E * sp.H;
-  const int csize = cluster_size(heads, sms * (ROWS == 16 ? 4 : 3));
+  const int csize = cluster_size(heads, sms * (ROWS == 16 ? 4 : 3), sp.b > sp.M ? sp.b : sp.M);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(heads * csize));
   cfg.blockDim = dim3(kThreads);

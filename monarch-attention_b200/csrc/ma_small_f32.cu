@@ -410,19 +410,20 @@ __global__ void __launch_bounds__(kThreads, 1) ma_small_f32_kernel(const Params 
   }
 }
 
-// CTAs per head (1, 2 or 4): waves of resident CTAs cost ceil(heads * C /
+// CTAs per head (1, 2, 4 or 8): waves of resident CTAs cost ceil(heads * C /
 // slots) / C of a head's work each, plus ~10 % per doubling of C for cluster
 // barriers and idle warps (a phase has only b or M items).  MA_SMALL_CLUSTER
 // overrides.
-static int cluster_size(int heads, int slots) {
+static int cluster_size(int heads, int slots, int items) {
   const char* env = getenv("MA_SMALL_CLUSTER");
   if (env) {
     const int c = atoi(env);
-    if (c == 1 || c == 2 || c == 4) return c;
+    if (c == 1 || c == 2 || c == 4 || c == 8) return c;
   }
   int best_c = 1;
   double best = 1e300;
-  for (int c = 1, lg = 0; c <= 4; c *= 2, ++lg) {
+  // up to 8 CTAs, while the cluster's warps have an item each in every phase
+  for (int c = 1, lg = 0; c <= 8 && (c == 1 || c * kWarps <= items); c *= 2, ++lg) {
     const int64_t waves = ((int64_t)heads * c + slots - 1) / slots;
     const double cost = (double)waves / c * (1.0 + 0.1 * lg);
     if (cost < best - 1e-9) {
@@ -450,7 +451,7 @@ static cudaError_t launch(const Params& sp, cudaStream_t st) {
   if (err != cudaSuccess) return err;
   if (per_sm < 1) per_sm = 1;
   const int heads = sp.E * sp.H;
-  const int csize = cluster_size(heads, sms * per_sm);
+  const int csize = cluster_size(heads, sms * per_sm, sp.b > sp.M ? sp.b : sp.M);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(heads * csize));
   cfg.blockDim = dim3(kThreads);

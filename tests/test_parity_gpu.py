@@ -175,7 +175,7 @@ def test_caller_layout_in_and_out(impl, shape, cuda_device):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
-@pytest.mark.parametrize("csize", ["1", "2", "4"])
+@pytest.mark.parametrize("csize", ["1", "2", "4", "8"])
 def test_small_kernel_cluster_sizes(csize, dtype, cuda_device, monkeypatch):
     """The small-block kernels (mma.sync 16-bit, FFMA fp32) split a head over a
     cluster of 1, 2 or 4 CTAs; every split gives the oracle's result (masked
